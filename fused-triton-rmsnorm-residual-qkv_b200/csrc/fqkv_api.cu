@@ -1,0 +1,392 @@
+// fqkv_api.cu -- the extern "C" boundary of the library (include/fused_rmsnorm_qkv.h).
+//
+// Validation happens before any CUDA call, so an invalid argument returns its error
+// code even on a machine without a GPU.  The library allocates nothing: schedules that
+// need scratch take it from the caller (fqkv_workspace_bytes).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fqkv_kernels.cuh"
+
+namespace fqkv {
+
+__device__ int g_status = 0;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  t_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return -static_cast<int>(e);
+}
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  bool init = false;
+  int major = 0, minor = 0, sms = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FQKV_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    if ((e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    d.init = true;
+  }
+  *out = d;
+  return 0;
+}
+
+// cuTensorMapEncodeTiled, reached through the runtime so the library does not link libcuda.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encode(EncodeTiledFn* fn) {
+  std::call_once(g_encode_once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!g_encode) return fail(FQKV_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+  *fn = g_encode;
+  return 0;
+}
+
+// 2-D K-major tensor map over a [rows, cols] matrix of 16-bit elements with row
+// stride ld (elements), 128-byte swizzle, box {64, box_rows}.
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+             bool bf16) {
+  EncodeTiledFn enc;
+  if (int rc = get_encode(&enc)) return rc;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FQKV_ERR_ALIGN, "cuTensorMapEncodeTiled failed (%d) for a [%lld, %lld] matrix, ld %lld", (int)r,
+                (long long)rows, (long long)cols, (long long)ld);
+  return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool overlaps(const void* a, int64_t a_bytes, const void* b, int64_t b_bytes) {
+  if (!a || !b) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + (uintptr_t)b_bytes && b0 < a0 + (uintptr_t)a_bytes;
+}
+
+int64_t mat_bytes(int64_t rows, int64_t cols, int64_t ld) { return ((rows - 1) * ld + cols) * 2; }
+
+// Bounds of the size-based automatic choice (M = tokens).
+constexpr int64_t kDecodeMaxM = 32;   // automatic choice of the fused decode kernel
+constexpr int64_t kFusedMaxM = 64;    // the fused kernel's limit when forced
+constexpr int64_t kSplitMaxM = 128;   // pre-pass + swap-AB GEMM
+constexpr int64_t kPrepassMaxH = 16384;
+
+struct Problem {
+  int64_t M, H, N, ldx, ldr, ldw, ldo, ldro;
+  const void *x, *r, *g, *w;
+  void *out, *rout;
+  int dtype, gdt, schedule, flags;
+};
+
+bool tma_eligible(const Problem& p) {
+  if (p.H % 8 || p.ldx % 8 || p.ldw % 8) return false;
+  if (p.r && p.ldr % 8) return false;
+  if (p.rout && p.ldro % 8) return false;
+  if (!aligned16(p.x) || !aligned16(p.w) || !aligned16(p.g) || (p.r && !aligned16(p.r)) ||
+      (p.rout && !aligned16(p.rout)))
+    return false;
+  if (p.H > kPrepassMaxH) return false;
+  return true;
+}
+
+int auto_schedule_for(int64_t M, int64_t H);
+
+int choose_schedule(const Problem& p) {
+  if (p.schedule != FQKV_SCHED_AUTO) return p.schedule;
+  if (!tma_eligible(p)) return FQKV_SCHED_SIMT;
+  return auto_schedule_for(p.M, p.H);
+}
+
+int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
+
+// Workspace layout: [normalised rows M x H][stream-K partial slots][stream-K counters].
+int64_t workspace_for(int sched, int64_t M, int64_t H, int64_t N) {
+  if (sched == FQKV_SCHED_PREFILL) return align256(M * H * 2);
+  if (sched == FQKV_SCHED_SPLIT)
+    return align256(M * H * 2) + align256(streamk_partials_bytes((int)M)) + align256(streamk_counters_bytes((int)N));
+  return 0;
+}
+
+int auto_schedule_for(int64_t M, int64_t H) {
+  if (H % 8 || H > kPrepassMaxH) return FQKV_SCHED_SIMT;
+  return M <= kDecodeMaxM ? FQKV_SCHED_DECODE : (M <= kSplitMaxM ? FQKV_SCHED_SPLIT : FQKV_SCHED_PREFILL);
+}
+
+int validate(const Problem& p) {
+  if (!p.x || !p.g || !p.w || !p.out)
+    return fail(FQKV_ERR_NULL, "x, rms_weight, weight and out must be non-null");
+  if (p.dtype != FQKV_F16 && p.dtype != FQKV_BF16)
+    return fail(FQKV_ERR_DTYPE, "dtype %d is not supported (fp16 = 0, bf16 = 1)", p.dtype);
+  if (p.gdt != FQKV_F16 && p.gdt != FQKV_BF16 && p.gdt != FQKV_F32)
+    return fail(FQKV_ERR_DTYPE, "rms_weight dtype %d is not supported", p.gdt);
+  if (p.M <= 0 || p.H <= 0 || p.N <= 0)
+    return fail(FQKV_ERR_SHAPE, "M, H and N must be positive (got %lld, %lld, %lld)", (long long)p.M,
+                (long long)p.H, (long long)p.N);
+  if (p.M > INT32_MAX || p.H > INT32_MAX || p.N > INT32_MAX)
+    return fail(FQKV_ERR_SHAPE, "M, H and N must be below 2^31");
+  if (p.ldx < p.H || p.ldw < p.H || p.ldo < p.N || (p.r && p.ldr < p.H) || (p.rout && p.ldro < p.H))
+    return fail(FQKV_ERR_SHAPE, "a row stride is smaller than its row length");
+  if (p.schedule < FQKV_SCHED_AUTO || p.schedule > FQKV_SCHED_PREFILL)
+    return fail(FQKV_ERR_SCHEDULE, "unknown schedule %d", p.schedule);
+  if (p.flags & ~(FQKV_FLAG_PDL | FQKV_FLAG_STATIC_WEIGHTS))
+    return fail(FQKV_ERR_SCHEDULE, "unknown flag bits 0x%x", p.flags);
+  const int64_t xb = mat_bytes(p.M, p.H, p.ldx), ob = mat_bytes(p.M, p.N, p.ldo);
+  const int64_t wb = mat_bytes(p.N, p.H, p.ldw);
+  const int64_t rb = p.r ? mat_bytes(p.M, p.H, p.ldr) : 0, rob = p.rout ? mat_bytes(p.M, p.H, p.ldro) : 0;
+  if (overlaps(p.out, ob, p.x, xb) || overlaps(p.out, ob, p.r, rb) || overlaps(p.out, ob, p.w, wb) ||
+      overlaps(p.out, ob, p.rout, rob))
+    return fail(FQKV_ERR_ALIAS, "out overlaps an input or residual_out");
+  if (overlaps(p.rout, rob, p.x, xb) || overlaps(p.rout, rob, p.r, rb) || overlaps(p.rout, rob, p.w, wb))
+    return fail(FQKV_ERR_ALIAS, "residual_out overlaps an input (in-place update is not supported)");
+  const int sched = choose_schedule(p);
+  if (sched != FQKV_SCHED_SIMT) {
+    if (!tma_eligible(p))
+      return fail(FQKV_ERR_ALIGN,
+                  "schedule %d needs H %% 8 == 0, H <= %lld, row strides %% 8 == 0 and 16-byte aligned x, "
+                  "residual, rms_weight, weight and residual_out",
+                  sched, (long long)kPrepassMaxH);
+    if (sched == FQKV_SCHED_DECODE && p.M > kFusedMaxM)
+      return fail(FQKV_ERR_SCHEDULE, "the decode schedule takes at most %lld rows (M = %lld)",
+                  (long long)kFusedMaxM, (long long)p.M);
+    if (sched == FQKV_SCHED_SPLIT && p.M > kSplitMaxM)
+      return fail(FQKV_ERR_SCHEDULE, "the split schedule takes at most %lld rows (M = %lld)",
+                  (long long)kSplitMaxM, (long long)p.M);
+  }
+  return 0;
+}
+
+}  // namespace
+}  // namespace fqkv
+
+using namespace fqkv;
+
+extern "C" FQKV_API int fqkv_version(void) { return 100; }
+
+extern "C" FQKV_API const char* fqkv_last_error(void) { return t_last_error.c_str(); }
+
+extern "C" FQKV_API int64_t fqkv_workspace_bytes(int64_t M, int64_t H, int64_t N, int dtype, int schedule) {
+  if (M <= 0 || H <= 0 || N <= 0) return -fail(FQKV_ERR_SHAPE, "M, H and N must be positive");
+  if (dtype != FQKV_F16 && dtype != FQKV_BF16) return -fail(FQKV_ERR_DTYPE, "unsupported dtype %d", dtype);
+  if (schedule < FQKV_SCHED_AUTO || schedule > FQKV_SCHED_PREFILL)
+    return -fail(FQKV_ERR_SCHEDULE, "unknown schedule %d", schedule);
+  const int sched = schedule == FQKV_SCHED_AUTO ? auto_schedule_for(M, H) : schedule;
+  return workspace_for(sched, M, H, N);
+}
+
+extern "C" FQKV_API int fqkv_query_schedule(int64_t M, int64_t H, int64_t N, int dtype, int schedule,
+                                   fqkv_schedule_info* info) {
+  if (!info) return fail(FQKV_ERR_NULL, "info must be non-null");
+  if (M <= 0 || H <= 0 || N <= 0) return fail(FQKV_ERR_SHAPE, "M, H and N must be positive");
+  if (dtype != FQKV_F16 && dtype != FQKV_BF16) return fail(FQKV_ERR_DTYPE, "unsupported dtype %d", dtype);
+  if (schedule < FQKV_SCHED_AUTO || schedule > FQKV_SCHED_PREFILL)
+    return fail(FQKV_ERR_SCHEDULE, "unknown schedule %d", schedule);
+  DeviceInfo d;
+  if (int rc = device_info(&d)) return rc;
+  const int sched = schedule == FQKV_SCHED_AUTO ? auto_schedule_for(M, H) : schedule;
+  std::memset(info, 0, sizeof(*info));
+  info->schedule = sched;
+  if (sched == FQKV_SCHED_SIMT) {
+    info->block_m = 8;
+    info->block_n = 64;
+    info->block_k = 64;
+    info->stages = 1;
+    info->split_k = 1;
+    info->grid = (int)(((N + 63) / 64) * ((M + 7) / 8));
+    info->threads = 256;
+    info->smem_bytes = (int)(sizeof(float) * (8 + 8 * 64 + 64 * 65));
+    return 0;
+  }
+  if (sched == FQKV_SCHED_DECODE) {
+    DecodeConfig c;
+    if (int rc = decode_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
+    info->block_m = c.mpad;
+    info->block_n = 128 * c.nt;
+    info->block_k = 64;
+    info->stages = c.stages;
+    info->split_k = c.cluster;
+    info->grid = (int)(((N + 128 * c.nt - 1) / (128 * c.nt)) * c.cluster);
+    info->threads = 192;
+    info->smem_bytes = (int)c.smem;
+    info->uses_prepass = 0;
+    return 0;
+  }
+  if (sched == FQKV_SCHED_SPLIT) {
+    StreamKConfig c;
+    if (int rc = streamk_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
+    info->block_m = c.mpad;
+    info->block_n = 128;
+    info->block_k = 64;
+    info->stages = c.stages;
+    info->split_k = 0;  // stream-K: ranges of (tile, k-block) units, not a fixed split
+    info->grid = c.grid;
+    info->threads = 192;
+    info->smem_bytes = (int)c.smem;
+    info->uses_prepass = 1;
+    return 0;
+  }
+  GemmConfig g;
+  if (int rc = gemm_pick_config((int)M, (int)H, (int)N, d.sms, &g)) return rc;
+  info->block_m = 128;
+  info->block_n = g.bn;
+  info->block_k = 64;
+  info->stages = g.stages;
+  info->split_k = 1;
+  info->grid = g.grid;
+  info->threads = 192;
+  info->smem_bytes = (int)g.smem;
+  info->uses_prepass = 1;
+  return 0;
+}
+
+extern "C" FQKV_API int fqkv_device_status(void* stream, int* status) {
+  if (!status) return fail(FQKV_ERR_NULL, "status must be non-null");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  int v = 0, zero = 0;
+  if ((e = cudaMemcpyFromSymbol(&v, g_status, sizeof(int))) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyFromSymbol");
+  if ((e = cudaMemcpyToSymbol(g_status, &zero, sizeof(int))) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyToSymbol");
+  *status = v;
+  return 0;
+}
+
+extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const void* rms_weight, int rms_weight_dtype,
+                           const void* weight, void* out, void* residual_out, int64_t M, int64_t H, int64_t N,
+                           int64_t ldx, int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro, float eps, int dtype,
+                           int schedule, int flags, void* workspace, int64_t workspace_bytes, void* stream) {
+  Problem p{M, H, N, ldx, ldr, ldw, ldo, ldro, x, residual, rms_weight, weight, out, residual_out,
+            dtype, rms_weight_dtype, schedule, flags};
+  if (int rc = validate(p)) return rc;
+  const int sched = choose_schedule(p);
+  const int64_t need = workspace_for(sched, M, H, N);
+  if (need > 0) {
+    if (!workspace || workspace_bytes < need)
+      return fail(FQKV_ERR_WORKSPACE, "schedule %d needs %lld bytes of workspace (got %lld)", sched,
+                  (long long)need, (long long)(workspace ? workspace_bytes : 0));
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+      return fail(FQKV_ERR_ALIGN, "workspace must be 256-byte aligned");
+  }
+  DeviceInfo d;
+  if (int rc = device_info(&d)) return rc;
+  if (d.major != 10) return fail(FQKV_ERR_DEVICE, "compute capability %d.%d is not sm_100", d.major, d.minor);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = dtype == FQKV_BF16;
+  const bool pdl = (flags & FQKV_FLAG_PDL) != 0;
+  const auto* xs = static_cast<const uint16_t*>(x);
+  const auto* rs = static_cast<const uint16_t*>(residual);
+  cudaError_t e = cudaSuccess;
+
+  if (sched == FQKV_SCHED_SIMT) {
+    SimtParams sp{xs, rs, rms_weight, rms_weight_dtype, static_cast<const uint16_t*>(weight),
+                  static_cast<uint16_t*>(out), static_cast<uint16_t*>(residual_out), M, H, N, ldx, ldr, ldw,
+                  ldo, ldro, eps};
+    e = launch_simt(sp, bf16, pdl, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "simt kernel launch");
+  }
+
+  uint16_t* normed = static_cast<uint16_t*>(workspace);
+  if (sched == FQKV_SCHED_DECODE) {
+    DecodeConfig c;
+    if (int rc = decode_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
+    CUtensorMap tmW;
+    if (int rc = make_map(&tmW, weight, N, H, ldw, 128 * c.nt, bf16)) return rc;
+    DecodeParams dp{xs, rs, rms_weight, rms_weight_dtype, static_cast<uint16_t*>(out),
+                    static_cast<uint16_t*>(residual_out), (int)M, (int)H, (int)N, ldx, ldr, ldo, ldro, eps,
+                    (int)((H + 63) / 64), 0, flags};
+    dp.nkb_max = (dp.kb_total + c.cluster - 1) / c.cluster;
+    e = launch_decode(c, tmW, dp, bf16, pdl, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "decode kernel launch");
+  }
+
+  // Pre-pass: updated residual + normalised rows (+ zeroed stream-K counters).
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int64_t normed_bytes = align256(M * H * 2);
+  float* partials = reinterpret_cast<float*>(ws + normed_bytes);
+  int* counters = reinterpret_cast<int*>(ws + normed_bytes + align256(streamk_partials_bytes((int)M)));
+  const int tiles128 = (int)((N + 127) / 128);
+  {
+    PrepassParams pp{xs, rs, rms_weight, rms_weight_dtype, static_cast<uint16_t*>(residual_out), normed, M, H,
+                     ldx, ldr, ldro, eps, sched == FQKV_SCHED_SPLIT ? counters : nullptr,
+                     sched == FQKV_SCHED_SPLIT ? tiles128 : 0};
+    e = launch_prepass(pp, bf16, pdl, st);
+    if (e != cudaSuccess) return cuda_fail(e, "norm pre-pass launch");
+  }
+
+  if (sched == FQKV_SCHED_SPLIT) {
+    StreamKConfig c;
+    if (int rc = streamk_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
+    CUtensorMap tmW, tmB;
+    if (int rc = make_map(&tmW, weight, N, H, ldw, 128, bf16)) return rc;
+    if (int rc = make_map(&tmB, normed, M, H, H, c.mpad, bf16)) return rc;
+    StreamKParams sp{static_cast<uint16_t*>(out), partials, counters, (int)M, (int)N, (int)H, ldo,
+                     (int)((H + 63) / 64), tiles128, flags};
+    // Chained to the pre-pass: the GEMM may start streaming the weight before the
+    // pre-pass finishes only if the caller declared the weight static.
+    e = launch_streamk(c, tmW, tmB, sp, bf16, true, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "stream-K GEMM launch");
+  }
+
+  GemmConfig g;
+  if (int rc = gemm_pick_config((int)M, (int)H, (int)N, d.sms, &g)) return rc;
+  CUtensorMap tmA, tmB;
+  if (int rc = make_map(&tmA, normed, M, H, H, 128, bf16)) return rc;
+  if (int rc = make_map(&tmB, weight, N, H, ldw, g.bn, bf16)) return rc;
+  GemmParams gp{static_cast<uint16_t*>(out), (int)M, (int)N, (int)H, ldo, (int)((H + 63) / 64),
+                (int)((M + 127) / 128), (int)((N + g.bn - 1) / g.bn), flags};
+  e = launch_gemm(g, tmA, tmB, gp, bf16, true, st);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "prefill GEMM launch");
+}

@@ -1,0 +1,440 @@
+// fqkv_decode.cu -- the fused small-M (decode) kernel: residual add, RMSNorm and the
+// projection in one launch, swap-AB tcgen05 GEMM with K split across a cluster.
+//
+// Decode (M = tokens <= 64) reads the whole weight once and little else, so it is
+// HBM-bound.  The kernel computes D^T = W * normed^T: a 128-row tile of the packed
+// weight is the MMA's A operand (M = 128) and the M tokens, padded to MPAD, are its
+// N operand, so the output features fill the tensor core's M dimension.
+//
+// Grid = (C, n_tiles), cluster = (C, 1, 1).  CTA `rank` of a cluster owns the
+// contiguous K slice [kb0, kb1) (64-element k-blocks) of n-tile blockIdx.y (NT x 128
+// weight rows).  Warp roles (192 threads):
+//   warp 0     TMA producer: streams the CTA's weight slice through a STAGES-deep
+//              ring of 128B-swizzled tiles (one TMA load per stage, no multicast).
+//   warp 1     TMEM allocator and single-thread MMA issuer (tcgen05.mma kind::f16,
+//              fp32 accumulators in TMEM, tcgen05.commit frees ring stages).
+//   warps 2-5  norm + epilogue.  Read x (+ residual) for the slice, form
+//              h = dtype(x + r) (bit-exact, baseline.py:48), write the updated residual
+//              (n-tile 0 only), keep h in shared memory in the UMMA operand layout,
+//              exchange per-row partial sums of squares across the cluster through
+//              DSMEM, then normalise in place: dtype((h * rstd) * g) (baseline.py:59-62).
+//              The normalised activations never leave shared memory.
+//              Epilogue: TMEM -> registers -> shared memory; the C partial sums of a
+//              tile are reduced through DSMEM in a fixed order (deterministic) and
+//              each CTA stores 1/C of the tile.
+// The host sizes (NT, C, STAGES) so that all clusters are resident at once
+// (cudaOccupancyMaxActiveClusters): a second wave would double the time.
+// Every wait is bounded (fqkv_device.cuh); after a timeout the kernel drains its own
+// TMA loads and MMAs, frees TMEM and returns with the status word set.
+#include <cstdlib>
+#include <mutex>
+#include <map>
+#include <tuple>
+#include <type_traits>
+
+#include "fqkv_kernels.cuh"
+
+namespace fqkv {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kMaxCluster = 8;
+constexpr int kTileRows = 128;      // rows of W per MMA (UMMA M)
+constexpr int kKBlock = 64;         // K elements per stage (128 bytes of 16-bit data)
+constexpr int kWTileBytes = kTileRows * 128;
+constexpr int kLoadBatch = 8;       // 16-byte chunks per lane loaded before any is used
+
+struct Layout {
+  uint32_t ring, stage_bytes, normed, red, rowp, rstd, bars, tmem_slot, total;
+};
+
+__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max) {
+  Layout L;
+  L.stage_bytes = nt * kWTileBytes;
+  L.ring = 0;
+  L.normed = L.ring + stages * L.stage_bytes;
+  L.red = L.normed + (uint32_t)nkb_max * mpad * 128;  // [kMaxCluster][mpad] floats
+  L.rowp = L.red + kMaxCluster * mpad * 4;            // [mpad] floats
+  L.rstd = L.rowp + mpad * 4;                         // [mpad] floats
+  L.bars = (L.rstd + mpad * 4 + 7) & ~7u;             // full[S], empty[S], accum, normed, sum, part
+  L.tmem_slot = L.bars + (2 * stages + 4) * 8;
+  L.total = L.tmem_slot + 16;
+  return L;
+}
+
+__host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
+  return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
+}
+
+template <typename T, int MPAD, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap tmW, const DecodeParams p, const int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Layout L = make_layout(stages, NT, MPAD, p.nkb_max);
+  uint8_t* ring = smem + L.ring;
+  uint8_t* normed = smem + L.normed;
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* rowp = reinterpret_cast<float*>(smem + L.rowp);
+  float* rstd_s = reinterpret_cast<float*>(smem + L.rstd);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + stages;
+  uint64_t* accum_bar = empty + stages;
+  uint64_t* normed_bar = accum_bar + 1;
+  uint64_t* sum_bar = accum_bar + 2;
+  uint64_t* part_bar = accum_bar + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
+  float* part = reinterpret_cast<float*>(ring);  // [NT][MPAD][128] partial tile, aliases the ring
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t C = gridDim.x;
+  const uint32_t rank = cluster_ctarank();
+  const int KB = p.kb_total;
+  const int kb0 = (int)((rank * (uint32_t)KB) / C), kb1 = (int)(((rank + 1) * (uint32_t)KB) / C);
+  const int nkb = kb1 - kb0;
+  const int n_base = blockIdx.y * NT * kTileRows;
+  constexpr uint32_t kTmemCols = tmem_cols_for(NT * MPAD);
+
+  // ---------------------------------------------------------------- setup
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum_bar, 1);
+    mbar_init(normed_bar, 1);
+    mbar_init(sum_bar, C * 32);
+    mbar_init(part_bar, C * 128);
+    fence_mbarrier_init_cluster();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmW);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  cluster_sync();  // every CTA of the cluster is running and has initialised its barriers
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint32_t tx = L.stage_bytes;
+      // The weight does not depend on the preceding grid when the caller says so: start
+      // streaming it before that grid has finished.
+      if (!(p.flags & FQKV_FLAG_STATIC_WEIGHTS)) pdl_wait();
+      const uint64_t pol_w = policy_evict_first();
+      bool ok = true;
+      int s = 0, round = 0, issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
+        mbar_arrive_expect_tx(&full[s], tx);
+        tma_load_2d_hint(ring + s * L.stage_bytes, &tmW, &full[s], (kb0 + i) * kKBlock, n_base, pol_w);
+        ++issued;
+        if (++s == stages) {
+          s = 0;
+          ++round;
+        }
+      }
+      // Before leaving, make sure none of this CTA's loads is still in flight: the last
+      // `stages` loads are the only ones that can be (bounded waits).
+      for (int j = max(0, issued - stages); j < issued; ++j) mbar_wait(&full[j % stages], (j / stages) & 1);
+      (void)ok;
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(kTileRows, MPAD, std::is_same<T, __nv_bfloat16>::value);
+      bool ok = mbar_wait(normed_bar, 0);
+      int s = 0, round = 0;
+      for (int i = 0; i < nkb && ok; ++i) {
+        if (!(ok = mbar_wait(&full[s], round & 1))) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(ring + s * L.stage_bytes);
+        const uint32_t b_base = smem_u32(normed + i * MPAD * 128);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t bdesc = make_sw128_desc(b_base + kk * 32);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint64_t adesc = make_sw128_desc(a_base + nt * kWTileBytes + kk * 32);
+            umma_f16(tmem_base + nt * MPAD, adesc, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&empty[s]);
+        if (++s == stages) {
+          s = 0;
+          ++round;
+        }
+      }
+      umma_commit(accum_bar);  // also on failure, so nobody waits for MMAs that never come
+      mbar_wait(accum_bar, 0);  // all MMAs retired before TMEM is freed
+    }
+  } else {
+    // ------------------------------------------------------------ norm + epilogue (warps 2..5)
+    const int et = threadIdx.x - 64;  // 0..127
+    bool ok = true;
+    pdl_wait();
+    const int nw = warp - 2;
+    const int nchunk = nkb * 8;  // 16-byte chunks per row of the slice
+    const int64_t k_lo = (int64_t)kb0 * kKBlock;
+    const bool write_res = p.rout != nullptr && blockIdx.y == 0;
+    // Pass 1: one warp per row; each lane issues kLoadBatch chunk loads of x (and r)
+    // before consuming any, so a row costs one memory latency per batch.
+    for (int m = nw; m < MPAD; m += 4) {
+      float ss = 0.f;
+      const bool live = m < p.M;
+      const uint16_t* xr = p.x + (int64_t)m * p.ldx;
+      const uint16_t* rr = p.r ? p.r + (int64_t)m * p.ldr : nullptr;
+      for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
+        uint4 xv[kLoadBatch], rv[kLoadBatch];
+#pragma unroll
+        for (int b = 0; b < kLoadBatch; ++b) {
+          const int j = j0 + lane + 32 * b;
+          const int64_t k = k_lo + (int64_t)j * 8;
+          xv[b] = make_uint4(0, 0, 0, 0);
+          rv[b] = make_uint4(0, 0, 0, 0);
+          if (live && j < nchunk && k < p.H) {
+            xv[b] = __ldg(reinterpret_cast<const uint4*>(xr + k));
+            if (rr) rv[b] = __ldg(reinterpret_cast<const uint4*>(rr + k));
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kLoadBatch; ++b) {
+          const int j = j0 + lane + 32 * b;
+          if (j >= nchunk) continue;
+          const int64_t k = k_lo + (int64_t)j * 8;
+          uint4 hv = xv[b];
+          if (live && k < p.H) {
+            if (rr) hv = add_rne8<T>(hv, rv[b]);
+            ss = sumsq8_acc<T>(hv, ss);
+            if (write_res) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
+          }
+          *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) rowp[m] = ss;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // Publish this CTA's per-row partial sums into slot `rank` of every CTA.
+    if (warp == 2) {
+      for (uint32_t c = 0; c < C; ++c) {
+        for (int m = lane; m < MPAD; m += 32)
+          st_cluster_f32(mapa_shared(smem_u32(&red[rank * MPAD + m]), c), rowp[m]);
+        mbar_arrive_remote(mapa_shared(smem_u32(sum_bar), c));
+      }
+    }
+    ok = mbar_wait<true>(sum_bar, 0);
+    for (int m = et; m < MPAD; m += 128) {
+      float tot = 0.f;
+      for (uint32_t c = 0; c < C; ++c) tot += red[c * MPAD + m];
+      rstd_s[m] = row_rstd(tot, p.H, p.eps);
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // Pass 2: normalise in place, dtype((h * rstd) * g).
+    for (int idx = et; idx < MPAD * nchunk; idx += 128) {
+      const int m = idx / nchunk, j = idx - m * nchunk;
+      const int64_t k = k_lo + (int64_t)j * 8;
+      if (m >= p.M || k >= p.H) continue;
+      uint4* ptr = reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
+      float4 gv[2];
+      load_gain8(p.g, p.gdt, k, gv);
+      *ptr = normalize8g<T>(*ptr, rstd_s[m], gv);
+    }
+    fence_proxy_async_smem();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (et == 0) mbar_arrive(normed_bar);
+
+    // Epilogue: TMEM -> registers -> this CTA's partial tile in shared memory.
+    ok = mbar_wait(accum_bar, 0) && ok;
+    tc_fence_after();
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int c0 = 0; c0 < MPAD; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + nt * MPAD + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) part[(nt * MPAD + c0 + e) * kTileRows + row] = __uint_as_float(v[e]);
+      }
+    }
+    tc_fence_before();
+    for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote(mapa_shared(smem_u32(part_bar), c));
+    ok = mbar_wait<true>(part_bar, 0) && ok;
+    // Reduce 1/C of the tile across the cluster (fixed order over ranks) and store it.
+    const int64_t total = (int64_t)NT * p.M * kTileRows;
+    const int64_t f0 = (rank * total) / C, f1 = ((rank + 1) * total) / C;
+    const uint32_t part_base = smem_u32(part);
+    for (int64_t f = f0 + et; f < f1; f += 128) {
+      const int nl = (int)(f % kTileRows);
+      const int64_t rest = f / kTileRows;
+      const int nt = (int)(rest % NT);
+      const int m = (int)(rest / NT);
+      const int n = n_base + nt * kTileRows + nl;
+      const uint32_t off = (uint32_t)(((nt * MPAD + m) * kTileRows + nl) * 4);
+      // All C peer loads are issued before the (fixed-order) sum.
+      float v[kMaxCluster];
+#pragma unroll
+      for (int c = 0; c < kMaxCluster; ++c) v[c] = (uint32_t)c < C ? ld_cluster_f32(mapa_shared(part_base + off, c)) : 0.f;
+      float acc = 0.f;
+#pragma unroll
+      for (int c = 0; c < kMaxCluster; ++c) acc += v[c];
+      if (n < p.N) p.out[(int64_t)m * p.ldo + n] = Elem<T>::from_f(acc);
+    }
+    (void)ok;
+  }
+
+  // ---------------------------------------------------------------- teardown
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while a peer may still read its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <int MPAD, int NT>
+auto kernel_ptr(bool bf16) {
+  return bf16 ? decode_kernel<__nv_bfloat16, MPAD, NT> : decode_kernel<__half, MPAD, NT>;
+}
+
+using KernelFn = void (*)(CUtensorMap, DecodeParams, int);
+
+KernelFn pick_kernel(int mpad, int nt, bool bf16) {
+  if (nt == 1) {
+    if (mpad == 16) return kernel_ptr<16, 1>(bf16);
+    if (mpad == 32) return kernel_ptr<32, 1>(bf16);
+    if (mpad == 64) return kernel_ptr<64, 1>(bf16);
+  } else {
+    if (mpad == 16) return kernel_ptr<16, 2>(bf16);
+    if (mpad == 32) return kernel_ptr<32, 2>(bf16);
+    if (mpad == 64) return kernel_ptr<64, 2>(bf16);
+  }
+  return nullptr;
+}
+
+cudaLaunchConfig_t base_config(const DecodeConfig& c, int tiles, cudaLaunchAttribute* attr, int* na) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)c.cluster, (unsigned)tiles);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = c.smem;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)c.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  *na = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// How many clusters of this configuration the device keeps resident at once (cached).
+int max_active_clusters(const DecodeConfig& c, int tiles) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, size_t>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, c.mpad, c.nt, c.cluster, c.smem);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  KernelFn k = pick_kernel(c.mpad, c.nt, true);
+  int n = 0;
+  if (k && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem) == cudaSuccess) {
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    cudaLaunchConfig_t cfg = base_config(c, tiles, attr, &na);
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+}  // namespace
+
+constexpr size_t kSmemLimit = 232448;  // max dynamic shared memory per block on sm_100
+
+size_t decode_smem_bytes(const DecodeConfig& c, int kb_total) {
+  const int nkb_max = (kb_total + c.cluster - 1) / c.cluster;
+  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max).total;
+}
+
+// Choose (tile rows, cluster size, ring depth).  Candidates must fit shared memory and
+// have every cluster resident at once; among them the one using the most SMs wins (ties
+// go to the deeper ring, then to the smaller cluster).
+// FQKV_DECODE_NT / FQKV_DECODE_CLUSTER / FQKV_DECODE_STAGES restrict the search.
+int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
+  DecodeConfig best{};
+  const int mpad = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
+  if (mpad == 0) return FQKV_ERR_SCHEDULE;
+  const int KB = (H + kKBlock - 1) / kKBlock;
+  const int force_nt = env_int("FQKV_DECODE_NT", 0);
+  const int force_c = env_int("FQKV_DECODE_CLUSTER", 0);
+  const int force_s = env_int("FQKV_DECODE_STAGES", 0);
+  long best_score = -1;
+  for (int nt = 1; nt <= 2; ++nt) {
+    if (force_nt && nt != force_nt) continue;
+    const int tiles = (N + nt * kTileRows - 1) / (nt * kTileRows);
+    for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
+      if (force_c && cl != force_c) continue;
+      // The epilogue's partial tile aliases the ring.
+      const int min_stages = (nt * mpad * kTileRows * 4 + nt * kWTileBytes - 1) / (nt * kWTileBytes);
+      for (int st = 16; st >= max(2, min_stages); --st) {
+        if (force_s && st != force_s) continue;
+        DecodeConfig t{mpad, nt, st, cl, 0};
+        t.smem = decode_smem_bytes(t, KB);
+        if (t.smem > kSmemLimit) continue;
+        const int resident = max_active_clusters(t, tiles);
+        if (resident < tiles) continue;  // would need a second wave
+        const long score = (long)tiles * cl * 64 + st;
+        if (score > best_score) {
+          best_score = score;
+          best = t;
+        }
+        break;  // deepest ring that fits for this (nt, cl)
+      }
+    }
+  }
+  if (best_score < 0) return FQKV_ERR_SCHEDULE;
+  *cfg = best;
+  return 0;
+}
+
+cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
+                          cudaStream_t stream) {
+  KernelFn k = pick_kernel(c.mpad, c.nt, bf16);
+  if (!k) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  const int tiles = (p.N + c.nt * kTileRows - 1) / (c.nt * kTileRows);
+  cudaLaunchConfig_t cfg = base_config(c, tiles, attr, &na);
+  cfg.stream = stream;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, k, tmW, p, c.stages);
+}
+
+}  // namespace fqkv

@@ -1,0 +1,205 @@
+// fqkv_kernels.cuh -- parameter blocks, element-wise helpers and host launcher
+// declarations shared by the kernels of the fused RMSNorm+QKV library.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "fqkv_device.cuh"
+
+namespace fqkv {
+
+// ------------------------------------------------------------------ parameters
+struct PrepassParams {
+  const uint16_t* x;
+  const uint16_t* r;  // nullable
+  const void* g;
+  int gdt;
+  uint16_t* rout;     // nullable
+  uint16_t* normed;   // [M, H], row stride H
+  int64_t M, H;
+  int64_t ldx, ldr, ldro;
+  float eps;
+  int* counters;      // nullable: zeroed by CTA 0 (the stream-K GEMM's arrival counters)
+  int n_counters;
+};
+
+struct SimtParams {
+  const uint16_t* x;
+  const uint16_t* r;  // nullable
+  const void* g;
+  int gdt;
+  const uint16_t* w;
+  uint16_t* out;
+  uint16_t* rout;     // nullable
+  int64_t M, H, N;
+  int64_t ldx, ldr, ldw, ldo, ldro;
+  float eps;
+};
+
+struct DecodeParams {
+  const uint16_t* x;
+  const uint16_t* r;  // nullable
+  const void* g;
+  int gdt;
+  uint16_t* out;
+  uint16_t* rout;     // nullable
+  int M, H, N;
+  int64_t ldx, ldr, ldo, ldro;
+  float eps;
+  int kb_total;       // ceil(H / 64)
+  int nkb_max;        // max k-blocks of one CTA's K slice
+  int flags;
+};
+
+struct StreamKParams {
+  uint16_t* out;
+  float* partials;    // [grid][2][MPAD][128] fp32 partial tiles
+  int* counters;      // [tiles] arrival counters, zero on entry
+  int M, N, H;
+  int64_t ldo;
+  int kb_total;
+  int tiles;
+  int flags;
+};
+
+struct GemmParams {
+  uint16_t* out;
+  int M, N, H;
+  int64_t ldo;
+  int kb_total;
+  int tiles_m, tiles_n;
+  int flags;
+};
+
+// ------------------------------------------------------------------ element helpers
+// h = dtype(fp32(x) + fp32(r)), round to nearest even: PyTorch's add of two
+// half-precision tensors (baseline.py:48).
+template <typename T>
+__device__ __forceinline__ uint16_t add_rne1(uint16_t a, uint16_t b) {
+  return Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(a), Elem<T>::to_f(b)));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t add_rne2(uint32_t a, uint32_t b) {
+  return (uint32_t)add_rne1<T>((uint16_t)(a & 0xFFFFu), (uint16_t)(b & 0xFFFFu)) |
+         ((uint32_t)add_rne1<T>((uint16_t)(a >> 16), (uint16_t)(b >> 16)) << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 add_rne8(uint4 a, uint4 b) {
+  return make_uint4(add_rne2<T>(a.x, b.x), add_rne2<T>(a.y, b.y), add_rne2<T>(a.z, b.z), add_rne2<T>(a.w, b.w));
+}
+
+// ss + sum of squares of the 8 elements, in element order.
+template <typename T>
+__device__ __forceinline__ float sumsq8_acc(uint4 v, float ss) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = Elem<T>::to_f((uint16_t)(w[i] & 0xFFFFu));
+    const float hi = Elem<T>::to_f((uint16_t)(w[i] >> 16));
+    ss = __fadd_rn(ss, __fmul_rn(lo, lo));
+    ss = __fadd_rn(ss, __fmul_rn(hi, hi));
+  }
+  return ss;
+}
+
+// dtype((fp32(h) * rstd) * fp32(g[k])), the order of baseline.py:61-62 / kernel.py:204.
+template <typename T>
+__device__ __forceinline__ uint16_t normalize1(uint16_t h, float rstd, float g) {
+  return Elem<T>::from_f(__fmul_rn(__fmul_rn(Elem<T>::to_f(h), rstd), g));
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 normalize8(uint4 h, float rstd, const void* g, int gdt, int64_t k) {
+  const uint32_t w[4] = {h.x, h.y, h.z, h.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint16_t lo = normalize1<T>((uint16_t)(w[i] & 0xFFFFu), rstd, load_gain(g, gdt, k + 2 * i));
+    const uint16_t hi = normalize1<T>((uint16_t)(w[i] >> 16), rstd, load_gain(g, gdt, k + 2 * i + 1));
+    o[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Gain elements k .. k+7 as fp32, one or two vector loads (k a multiple of 8; the gain
+// row is 16-byte aligned).
+__device__ __forceinline__ void load_gain8(const void* g, int gdt, int64_t k, float4 (&out)[2]) {
+  if (gdt == FQKV_F32) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + k);
+    out[0] = __ldg(p);
+    out[1] = __ldg(p + 1);
+    return;
+  }
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(g) + k));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint16_t lo = (uint16_t)(w[i] & 0xFFFFu), hi = (uint16_t)(w[i] >> 16);
+    f[2 * i] = gdt == FQKV_BF16 ? Elem<__nv_bfloat16>::to_f(lo) : Elem<__half>::to_f(lo);
+    f[2 * i + 1] = gdt == FQKV_BF16 ? Elem<__nv_bfloat16>::to_f(hi) : Elem<__half>::to_f(hi);
+  }
+  out[0] = make_float4(f[0], f[1], f[2], f[3]);
+  out[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
+// normalize8 with the gain already in registers.
+template <typename T>
+__device__ __forceinline__ uint4 normalize8g(uint4 h, float rstd, const float4 (&g)[2]) {
+  const float gf[8] = {g[0].x, g[0].y, g[0].z, g[0].w, g[1].x, g[1].y, g[1].z, g[1].w};
+  const uint32_t w[4] = {h.x, h.y, h.z, h.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint16_t lo = normalize1<T>((uint16_t)(w[i] & 0xFFFFu), rstd, gf[2 * i]);
+    const uint16_t hi = normalize1<T>((uint16_t)(w[i] >> 16), rstd, gf[2 * i + 1]);
+    o[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_prepass(const PrepassParams& p, bool bf16, bool pdl, cudaStream_t stream);
+cudaError_t launch_simt(const SimtParams& p, bool bf16, bool pdl, cudaStream_t stream);
+
+// Fused decode schedule chosen on the host.
+struct DecodeConfig {
+  int mpad;     // token columns of the MMA (16, 32 or 64)
+  int nt;       // 128-row W tiles per CTA (1 or 2)
+  int stages;   // ring depth
+  int cluster;  // CTAs splitting K (cluster size)
+  size_t smem;  // dynamic shared memory bytes
+};
+
+int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg);
+size_t decode_smem_bytes(const DecodeConfig& c, int kb_total);
+cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
+                          cudaStream_t stream);
+
+constexpr int kStreamKMaxGrid = 160;  // partial-slot capacity of the workspace (>= SM count)
+struct StreamKConfig {
+  int mpad;
+  int stages;
+  int grid;
+  size_t smem;
+};
+int streamk_mpad(int M);
+int64_t streamk_partials_bytes(int M);
+int64_t streamk_counters_bytes(int N);
+int streamk_pick_config(int M, int H, int N, int sm_count, StreamKConfig* cfg);
+cudaError_t launch_streamk(const StreamKConfig& c, const CUtensorMap& tmW, const CUtensorMap& tmB,
+                           const StreamKParams& p, bool bf16, bool pdl, cudaStream_t stream);
+
+struct GemmConfig {
+  int bn;       // output features per tile (MMA N)
+  int stages;
+  int grid;
+  size_t smem;
+};
+int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg);
+cudaError_t launch_gemm(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
+                        bool bf16, bool pdl, cudaStream_t stream);
+
+}  // namespace fqkv

@@ -1,0 +1,127 @@
+"""ctypes binding of ``libfqkv.so`` (C ABI declared in ``include/fused_rmsnorm_qkv.h``).
+
+The library is built in-tree by ``build.py`` next to this file.  Loading it never
+falls back to anything else: if the shared object is missing the import of the GPU
+entry points raises, with the build command in the message.
+
+Error mapping of ``fqkv_launch`` return codes:
+  FQKV_ERR_DTYPE -> TypeError, other codes > 0 -> ValueError, codes < 0 (CUDA
+  runtime errors) -> RuntimeError.  The message is ``fqkv_last_error()``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+# Constants mirrored from include/fused_rmsnorm_qkv.h.
+F16, BF16, F32 = 0, 1, 2
+SCHED_AUTO, SCHED_SIMT, SCHED_DECODE, SCHED_SPLIT, SCHED_PREFILL = -1, 0, 1, 2, 3
+FLAG_PDL, FLAG_STATIC_WEIGHTS = 1, 2
+ERR_NULL, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_WORKSPACE, ERR_SCHEDULE, ERR_DEVICE, ERR_DEVICE_TIMEOUT, ERR_ALIAS = (
+    1, 2, 3, 4, 5, 6, 7, 8, 9)
+STATUS_WAIT_TIMEOUT = 1
+
+SCHEDULE_NAMES = {SCHED_SIMT: "simt", SCHED_DECODE: "decode", SCHED_SPLIT: "split", SCHED_PREFILL: "prefill"}
+SCHEDULE_BY_NAME = {v: k for k, v in SCHEDULE_NAMES.items()}
+SCHEDULE_BY_NAME["auto"] = SCHED_AUTO
+SCHEDULE_BY_NAME["naive"] = SCHED_SIMT
+
+LIB_PATH = Path(__file__).resolve().parent / "libfqkv.so"
+
+EXPORTED_SYMBOLS = (
+    "fqkv_launch",
+    "fqkv_workspace_bytes",
+    "fqkv_query_schedule",
+    "fqkv_last_error",
+    "fqkv_device_status",
+    "fqkv_version",
+)
+
+
+class ScheduleInfo(ctypes.Structure):
+    """``fqkv_schedule_info``."""
+
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "schedule", "block_m", "block_n", "block_k", "stages", "split_k", "grid", "threads",
+        "smem_bytes", "uses_prepass")]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library, declaring every entry point's signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("FQKV_LIB", LIB_PATH))
+    if not path.exists():
+        raise RuntimeError(
+            f"{path} is missing: build the CUDA library first "
+            f"(python {Path(__file__).resolve().parent.parent / 'build.py'})")
+    lib = ctypes.CDLL(str(path))
+    i64, i32, vp, f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_float
+    lib.fqkv_launch.argtypes = [vp, vp, vp, i32, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, f32, i32,
+                                i32, i32, vp, i64, vp]
+    lib.fqkv_launch.restype = i32
+    lib.fqkv_workspace_bytes.argtypes = [i64, i64, i64, i32, i32]
+    lib.fqkv_workspace_bytes.restype = i64
+    lib.fqkv_query_schedule.argtypes = [i64, i64, i64, i32, i32, ctypes.POINTER(ScheduleInfo)]
+    lib.fqkv_query_schedule.restype = i32
+    lib.fqkv_last_error.argtypes = []
+    lib.fqkv_last_error.restype = ctypes.c_char_p
+    lib.fqkv_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
+    lib.fqkv_device_status.restype = i32
+    lib.fqkv_version.argtypes = []
+    lib.fqkv_version.restype = i32
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    return load().fqkv_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str = "fqkv_launch") -> None:
+    """Raise the Python exception matching a C-ABI return code."""
+    if rc == 0:
+        return
+    msg = f"{what}: {last_error()} (code {rc})"
+    if rc == ERR_DTYPE:
+        raise TypeError(msg)
+    if rc > 0:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw, ldo, ldro, eps,
+           dtype, schedule, flags, ws_ptr, ws_bytes, stream) -> int:
+    return load().fqkv_launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw,
+                              ldo, ldro, ctypes.c_float(eps), dtype, schedule, flags, ws_ptr, ws_bytes, stream)
+
+
+def workspace_bytes(M: int, H: int, N: int, dtype: int, schedule: int) -> int:
+    n = load().fqkv_workspace_bytes(M, H, N, dtype, schedule)
+    if n < 0:
+        check(-n, "fqkv_workspace_bytes")
+    return n
+
+
+def query_schedule(M: int, H: int, N: int, dtype: int, schedule: int = SCHED_AUTO) -> dict:
+    info = ScheduleInfo()
+    check(load().fqkv_query_schedule(M, H, N, dtype, schedule, ctypes.byref(info)), "fqkv_query_schedule")
+    return info.as_dict()
+
+
+def device_status(stream: int) -> int:
+    v = ctypes.c_int(0)
+    check(load().fqkv_device_status(stream, ctypes.byref(v)), "fqkv_device_status")
+    return v.value
+
+
+def version() -> int:
+    return load().fqkv_version()

@@ -1,0 +1,281 @@
+"""Fused residual add + RMSNorm + packed projection on B200 (sm_100a).
+
+Drop-in for the reference's ``src/triton_fused_rmsnorm_qkv/kernel.py``: the same public
+functions with the same arguments, return values and assertion errors, backed by
+hand-written sm_100a CUDA kernels in ``libfqkv.so`` instead of Triton.
+
+    hidden = x + residual                          (or x when residual is None)
+    normed = dtype((fp32(hidden) * rstd) * fp32(rms_weight)),  rstd = 1/sqrt(mean(hidden^2) + eps)
+    out    = normed @ weight^T                     (fp32 accumulation, output in x.dtype)
+
+Where the reference dispatches between two Triton kernels at M = 32 rows
+(kernel.py:360, :406) and picks tiles by autotuning (kernel.py:122-128, :264-268), the
+library chooses one of its kernel families from (M, H, N, SM count):
+
+* ``decode``  (M <= 32): one fused kernel -- swap-AB tcgen05 MMA, the weight streamed
+  by TMA, K split across a thread-block cluster whose CTAs exchange row sums of
+  squares and partial tiles through distributed shared memory.
+* ``split``   (32 < M <= 128): norm pre-pass + the same swap-AB GEMM reading the
+  normalised rows by TMA.
+* ``prefill`` (M > 128): norm pre-pass + persistent 128 x BN tcgen05 GEMM.
+* ``simt``    any shape/stride the TMA paths cannot take (H % 8 != 0, unaligned data).
+
+Extensions (keyword-only, so the reference call sites keep working): ``residual_out``
+receives the updated residual ``x + residual`` (bit-exact in the working dtype),
+``schedule`` forces a kernel family, ``static_weights`` lets the decode kernel start
+streaming the weight before the preceding kernel in the stream has finished.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+# The reference switches kernels at M = 32 (kernel.py:360).  The B200 dispatch lives in
+# the C library; these mirror its bounds for readers of the Python API.
+_PERSISTENT_THRESHOLD = 32
+_DECODE_MAX_M = 32
+_SPLIT_MAX_M = 128
+
+_DTYPE_CODE = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+_GAIN_CODE = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+
+# (M, H) -> N of the last call, so get_autotune_best_config(M, H) can describe the
+# schedule the library chose for it (the reference reads Triton's autotune cache).
+_seen_shapes: dict[tuple[int, int], int] = {}
+
+
+def _env_flag(name: str) -> bool:
+    return os.environ.get(name, "") not in ("", "0", "false", "False")
+
+
+def _schedule_code(schedule) -> int:
+    if schedule is None:
+        forced = os.environ.get("FQKV_FORCE_SCHEDULE", "")
+        return _lib.SCHEDULE_BY_NAME[forced] if forced else _lib.SCHED_AUTO
+    if isinstance(schedule, str):
+        if schedule not in _lib.SCHEDULE_BY_NAME:
+            raise ValueError(f"unknown schedule {schedule!r}; expected one of {sorted(_lib.SCHEDULE_BY_NAME)}")
+        return _lib.SCHEDULE_BY_NAME[schedule]
+    return int(schedule)
+
+
+def _rows(t: torch.Tensor, M: int, H: int) -> torch.Tensor:
+    """View ``t`` as [M, H] with unit column stride (copying only if it must)."""
+    t2 = t.reshape(M, H)
+    if t2.stride(1) != 1:
+        t2 = t2.contiguous()
+    return t2
+
+
+def _launch(x2: torch.Tensor, r2: Optional[torch.Tensor], rms_weight: torch.Tensor, weight: torch.Tensor,
+            out2: torch.Tensor, rout2: Optional[torch.Tensor], eps: float, schedule: int,
+            static_weights: bool) -> None:
+    """Validate tensor metadata and call ``fqkv_launch`` on the current stream."""
+    M, H = x2.shape
+    N = weight.shape[0]
+    if x2.dtype not in _DTYPE_CODE:
+        raise TypeError(f"x must be float16 or bfloat16, got {x2.dtype}")
+    if weight.dtype != x2.dtype:
+        raise TypeError(f"weight dtype {weight.dtype} does not match x dtype {x2.dtype}")
+    if r2 is not None and r2.dtype != x2.dtype:
+        raise TypeError(f"residual dtype {r2.dtype} does not match x dtype {x2.dtype}")
+    if rms_weight.dtype not in _GAIN_CODE:
+        raise TypeError(f"rms_weight must be float32, float16 or bfloat16, got {rms_weight.dtype}")
+    if rms_weight.numel() != H:
+        raise ValueError(f"rms_weight must have H={H} elements, got shape {tuple(rms_weight.shape)}")
+    dev = x2.device
+    for name, t in (("residual", r2), ("rms_weight", rms_weight), ("weight", weight)):
+        if t is not None and t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, x is on {dev}")
+    g = rms_weight.reshape(H)
+    if g.stride(0) != 1:
+        g = g.contiguous()
+    w = weight if weight.stride(1) == 1 else weight.contiguous()
+    code = _schedule_code(schedule)
+    flags = _lib.FLAG_PDL
+    if static_weights:
+        flags |= _lib.FLAG_STATIC_WEIGHTS
+    with torch.cuda.device(dev):
+        ws_bytes = _lib.workspace_bytes(M, H, N, _DTYPE_CODE[x2.dtype], code)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = _lib.launch(
+            x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), _GAIN_CODE[g.dtype],
+            w.data_ptr(), out2.data_ptr(), rout2.data_ptr() if rout2 is not None else None,
+            M, H, N, x2.stride(0), r2.stride(0) if r2 is not None else 0, w.stride(0), out2.stride(0),
+            rout2.stride(0) if rout2 is not None else 0, float(eps), _DTYPE_CODE[x2.dtype], code, flags,
+            ws.data_ptr() if ws is not None else None, ws_bytes, stream)
+    _lib.check(rc)
+    _seen_shapes[(M, H)] = N
+
+
+def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, static_weights):
+    assert x.is_cuda, "Fused kernel requires CUDA tensors"
+    B, S, H = x.shape
+    N_OUT = weight.shape[0]
+    assert weight.shape[1] == H, f"weight must be (N_OUT, H); got {weight.shape} for H={H}"
+    M = B * S
+    x2 = _rows(x, M, H)
+    r2 = None
+    if residual is not None:
+        if residual.numel() != M * H:
+            raise ValueError(f"residual must match x {tuple(x.shape)}, got {tuple(residual.shape)}")
+        r2 = _rows(residual, M, H)
+    out = torch.empty(M, N_OUT, dtype=x.dtype, device=x.device)
+    rout2 = None
+    if residual_out is not None:
+        if residual_out.numel() != M * H or residual_out.dtype != x.dtype or residual_out.device != x.device:
+            raise ValueError("residual_out must have the shape, dtype and device of x")
+        rout2 = residual_out.view(M, H)
+        if rout2.stride(1) != 1:
+            raise ValueError("residual_out must have unit stride along H")
+    if static_weights is None:
+        static_weights = _env_flag("FQKV_STATIC_WEIGHTS")
+    _launch(x2, r2, rms_weight, weight, out, rout2, eps, schedule, static_weights)
+    return out.reshape(B, S, N_OUT)
+
+
+def fused_rmsnorm_residual_matmul(
+    x: torch.Tensor,
+    residual: Optional[torch.Tensor],
+    rms_weight: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float = 1e-6,
+    *,
+    residual_out: Optional[torch.Tensor] = None,
+    schedule=None,
+    static_weights: Optional[bool] = None,
+) -> torch.Tensor:
+    """Fused (optional residual) + RMSNorm + arbitrary-width matmul (kernel.py:363-436).
+
+    Args:
+        x: (B, S, H) activations, float16 or bfloat16.
+        residual: (B, S, H) residual stream, or None to skip the add.
+        rms_weight: (H,) RMSNorm gain (float32, float16 or bfloat16).
+        weight: (N_OUT, H) projection, e.g. the packed GQA weight [Wq; Wk; Wv].
+        eps: RMSNorm epsilon.
+        residual_out: optional (B, S, H) tensor that receives x + residual.
+        schedule: None/"auto", "decode", "split", "prefill" or "simt" ("naive").
+        static_weights: weight is not written by the preceding kernel in the stream
+            (default: environment variable FQKV_STATIC_WEIGHTS).
+
+    Returns:
+        (B, S, N_OUT) tensor in x.dtype.
+    """
+    return _fused(x, residual, rms_weight, weight, eps, residual_out=residual_out, schedule=schedule,
+                  static_weights=static_weights)
+
+
+def fused_add_rmsnorm_matmul(
+    x: torch.Tensor,
+    residual: Optional[torch.Tensor],
+    rms_weight: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float = 1e-6,
+    *,
+    return_residual: bool = True,
+    schedule=None,
+    static_weights: Optional[bool] = None,
+):
+    """As ``fused_rmsnorm_residual_matmul``, also returning the updated residual.
+
+    Returns ``(out, hidden)`` with ``hidden = x + residual`` computed once in fp32 and
+    rounded to x.dtype (bit-identical to ``x + residual`` in PyTorch, baseline.py:48),
+    or ``out`` alone when ``return_residual`` is False.
+    """
+    hidden = torch.empty_like(x) if return_residual else None
+    out = _fused(x, residual, rms_weight, weight, eps, residual_out=hidden, schedule=schedule,
+                 static_weights=static_weights)
+    return (out, hidden) if return_residual else out
+
+
+def fused_rmsnorm_residual_qkv(
+    x: torch.Tensor,
+    residual: Optional[torch.Tensor],
+    rms_weight: torch.Tensor,
+    qkv_weight: torch.Tensor,
+    eps: float = 1e-6,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """MHA convenience wrapper for a (3*H, H) packed weight (kernel.py:439-461).
+
+    For GQA call ``fused_rmsnorm_residual_matmul`` with the (H + 2*H_kv, H) weight and
+    split the result by the real widths.
+    """
+    H = x.shape[-1]
+    assert qkv_weight.shape == (3 * H, H), (
+        f"qkv_weight must be (3*H, H); got {qkv_weight.shape}. "
+        "For GQA, call fused_rmsnorm_residual_matmul directly."
+    )
+    out = fused_rmsnorm_residual_matmul(x, residual, rms_weight, qkv_weight, eps)
+    q, k, v = out.chunk(3, dim=-1)
+    return q, k, v
+
+
+def fused_rmsnorm_residual_matmul_fixed(
+    x: torch.Tensor,
+    residual: Optional[torch.Tensor],
+    rms_weight: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float = 1e-6,
+) -> torch.Tensor:
+    """Same contract with the adaptive dispatch switched off (kernel.py:469-540).
+
+    The reference pins one untuned Triton tile for its autotune ablation; here every
+    shape runs the fixed-tile CUDA-core ("simt") kernel.
+    """
+    assert x.is_cuda
+    B, S, H = x.shape
+    assert weight.shape[1] == H
+    return _fused(x, residual, rms_weight, weight, eps, residual_out=None, schedule=_lib.SCHED_SIMT,
+                  static_weights=False)
+
+
+def fused_rmsnorm_residual_qkv_fixed(
+    x: torch.Tensor,
+    residual: Optional[torch.Tensor],
+    rms_weight: torch.Tensor,
+    qkv_weight: torch.Tensor,
+    eps: float = 1e-6,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Same interface as ``fused_rmsnorm_residual_qkv`` with the dispatch off (kernel.py:543-555)."""
+    H = x.shape[-1]
+    assert qkv_weight.shape == (3 * H, H)
+    out = fused_rmsnorm_residual_matmul_fixed(x, residual, rms_weight, qkv_weight, eps)
+    q, k, v = out.chunk(3, dim=-1)
+    return q, k, v
+
+
+def get_autotune_best_config(M: int, H: int) -> dict | None:
+    """Describe the schedule chosen for a (M, H) seen before, else None (kernel.py:558-572).
+
+    Keys ``BLOCK_M``, ``BLOCK_N``, ``BLOCK_K``, ``num_warps`` and ``num_stages`` carry
+    the reference's meaning; ``schedule``, ``split_k``, ``grid`` and ``smem_bytes``
+    describe the B200 kernel.
+    """
+    N = _seen_shapes.get((M, H))
+    if N is None or not torch.cuda.is_available():
+        return None
+    info = _lib.query_schedule(M, H, N, _lib.BF16)
+    return {
+        "BLOCK_M": info["block_m"],
+        "BLOCK_N": info["block_n"],
+        "BLOCK_K": info["block_k"],
+        "num_warps": info["threads"] // 32,
+        "num_stages": info["stages"],
+        "schedule": _lib.SCHEDULE_NAMES.get(info["schedule"], str(info["schedule"])),
+        "split_k": info["split_k"],
+        "grid": info["grid"],
+        "smem_bytes": info["smem_bytes"],
+        "uses_prepass": bool(info["uses_prepass"]),
+    }
+
+
+def device_status(device=None) -> int:
+    """Synchronise the current stream and return/clear the library's device status bits."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        return _lib.device_status(torch.cuda.current_stream(dev).cuda_stream)

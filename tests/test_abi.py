@@ -1,0 +1,122 @@
+"""The C-ABI library: it loads, exports every entry point include/*.h declares, and
+rejects invalid arguments with the documented codes before touching CUDA.  CPU only
+(no kernel is launched: every call here fails validation first)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from triton_fused_rmsnorm_qkv import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_symbols() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        for m in re.finditer(r"FQKV_API\s+[\w\s\*]+?\b(fqkv_\w+)\s*\(", h.read_text()):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_the_abi():
+    assert declared_symbols() == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert _lib.version() == 100
+
+
+FAKE = 0x100000  # 16-byte aligned, never dereferenced: validation fails before any launch
+
+
+def call(**kw):
+    a = dict(x=FAKE, r=FAKE * 2, g=FAKE * 3, gdt=_lib.BF16, w=FAKE * 4, out=FAKE * 64, rout=None,
+             M=4, H=256, N=512, ldx=256, ldr=256, ldw=256, ldo=512, ldro=256, eps=1e-5, dtype=_lib.BF16,
+             schedule=_lib.SCHED_AUTO, flags=0, ws=None, ws_bytes=0, stream=None)
+    a.update(kw)
+    # Keep fake buffers far apart so only the aliasing tests alias.
+    return _lib.launch(a["x"], a["r"], a["g"], a["gdt"], a["w"], a["out"], a["rout"], a["M"], a["H"], a["N"],
+                       a["ldx"], a["ldr"], a["ldw"], a["ldo"], a["ldro"], a["eps"], a["dtype"], a["schedule"],
+                       a["flags"], a["ws"], a["ws_bytes"], a["stream"])
+
+
+SPACED = dict(x=1 << 32, r=2 << 32, g=3 << 32, w=4 << 32, out=5 << 32)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(x=None), _lib.ERR_NULL),
+    (dict(g=None), _lib.ERR_NULL),
+    (dict(w=None), _lib.ERR_NULL),
+    (dict(out=None), _lib.ERR_NULL),
+    (dict(dtype=2), _lib.ERR_DTYPE),
+    (dict(dtype=7), _lib.ERR_DTYPE),
+    (dict(gdt=5), _lib.ERR_DTYPE),
+    (dict(M=0), _lib.ERR_SHAPE),
+    (dict(H=0), _lib.ERR_SHAPE),
+    (dict(N=-3), _lib.ERR_SHAPE),
+    (dict(ldx=100), _lib.ERR_SHAPE),
+    (dict(ldw=255), _lib.ERR_SHAPE),
+    (dict(ldo=511), _lib.ERR_SHAPE),
+    (dict(ldr=128), _lib.ERR_SHAPE),
+    (dict(M=1 << 31), _lib.ERR_SHAPE),
+    (dict(schedule=9), _lib.ERR_SCHEDULE),
+    (dict(flags=64), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_DECODE, M=65), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_SPLIT, M=129), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_DECODE, H=260, ldx=260, ldr=260, ldw=260, ldro=260), _lib.ERR_ALIGN),
+    (dict(schedule=_lib.SCHED_DECODE, x=(1 << 32) + 2), _lib.ERR_ALIGN),
+    (dict(schedule=_lib.SCHED_PREFILL, M=4096, ws=None), _lib.ERR_WORKSPACE),
+    (dict(schedule=_lib.SCHED_PREFILL, M=4096, ws=6 << 32, ws_bytes=1024), _lib.ERR_WORKSPACE),
+    (dict(schedule=_lib.SCHED_PREFILL, M=4096, ws=(6 << 32) + 16, ws_bytes=1 << 30), _lib.ERR_ALIGN),
+    (dict(out=(1 << 32) + 64), _lib.ERR_ALIAS),
+    (dict(rout=(2 << 32) + 64), _lib.ERR_ALIAS),
+])
+def test_invalid_arguments_are_rejected(kw, code):
+    args = dict(SPACED)
+    args.update(kw)
+    assert call(**args) == code
+    assert _lib.last_error() != ""
+
+
+def test_python_error_mapping():
+    with pytest.raises(TypeError):
+        _lib.check(_lib.ERR_DTYPE)
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_SHAPE)
+    with pytest.raises(RuntimeError):
+        _lib.check(-1)
+
+
+def _split_bytes(M, H, N):
+    """Normalised rows + stream-K partial slots (160 CTAs x 2 x MPAD x 128 fp32) + counters."""
+    a = lambda b: (b + 255) // 256 * 256  # noqa: E731
+    mpad = 16 if M <= 16 else 32 if M <= 32 else 64 if M <= 64 else 128
+    return a(M * H * 2) + a(160 * 2 * mpad * 128 * 4) + a(((N + 127) // 128) * 4)
+
+
+@pytest.mark.parametrize("M,H,sched,expect", [
+    (1, 4096, _lib.SCHED_AUTO, 0),                  # fused decode: no scratch
+    (16, 4096, _lib.SCHED_DECODE, 0),
+    (64, 4096, _lib.SCHED_AUTO, _split_bytes(64, 4096, 6144)),   # pre-pass + stream-K
+    (16, 4096, _lib.SCHED_SPLIT, _split_bytes(16, 4096, 6144)),
+    (2048, 4096, _lib.SCHED_PREFILL, 2048 * 4096 * 2),           # pre-pass scratch only
+    (7, 4100, _lib.SCHED_AUTO, 0),                  # H % 8 != 0 -> SIMT, no scratch
+    (3, 100, _lib.SCHED_SIMT, 0),
+])
+def test_workspace_sizes(M, H, sched, expect):
+    assert _lib.workspace_bytes(M, H, 6144, _lib.BF16, sched) == expect
+
+
+def test_workspace_size_rejects_bad_arguments():
+    with pytest.raises(ValueError):
+        _lib.workspace_bytes(0, 4096, 6144, _lib.BF16, -1)
+    with pytest.raises(TypeError):
+        _lib.workspace_bytes(4, 4096, 6144, 9, -1)

@@ -1,0 +1,216 @@
+"""Parity of the CUDA kernels with the CPU oracle (restated baseline.py).
+
+Bars (the benchmark contract): Q/K/V max-abs error <= 2e-2 and relative L2 error
+<= 5e-3 against the oracle on the same seeded inputs; the updated residual bit-exact.
+bf16 cannot represent a 2e-2 difference above |x| = 4 (its ulp there is 0.03125), and a
+kernel whose fp32 summation order differs from the CPU BLAS rounds the odd such output
+to the neighbouring bf16 value; so every element is held to max(2e-2, 1 ulp of the
+reference) (``within_bars``) and, separately, the output must be a faithful rounding of
+the unrounded fp32 product (``faithful_rounding_metrics``: within 0.6 ulp + 2e-3).
+Full-size configs compare a random sample of rows (rows are independent, so a sampled
+row is checked exactly as it would be in a full comparison) to keep the CPU oracle to
+seconds.  All tests call the library through its public API / C ABI.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import faithful_rounding_metrics, forward, make_case, parity_metrics, rms_normalize, within_bars
+from triton_fused_rmsnorm_qkv import _lib, fused_add_rmsnorm_matmul, fused_rmsnorm_residual_matmul
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+REL_L2 = 5e-3
+
+
+def run_case(M, H, N, dtype, seed, res=True, eps=1e-5, schedule=None, sample_rows=None, gain_dtype=None,
+             static_weights=False):
+    x, r, g, w = make_case(M, H, N, dtype, seed, res, gain_dtype=gain_dtype)
+    dev = "cuda"
+    out, hidden = fused_add_rmsnorm_matmul(
+        x.to(dev)[None], r.to(dev)[None] if r is not None else None, g.to(dev), w.to(dev), eps,
+        schedule=schedule, static_weights=static_weights)
+    torch.cuda.synchronize()
+    out, hidden = out[0].cpu(), hidden[0].cpu()
+    rows = torch.arange(M)
+    if sample_rows is not None and sample_rows < M:
+        rows = torch.randperm(M, generator=torch.Generator().manual_seed(seed))[:sample_rows].sort().values
+    xs, rs = x[rows], (r[rows] if r is not None else None)
+    acc = "native" if M * N * H <= 64 * 6144 * 4096 else "fp32"
+    ref_out, ref_hidden = forward(xs, rs, g, w, eps, accumulate=acc)
+    m = parity_metrics(out[rows], ref_out)
+    assert within_bars(m, MAX_ABS, REL_L2), m
+    exact = torch.nn.functional.linear(rms_normalize(ref_hidden, g, eps).float(), w.float())
+    f = faithful_rounding_metrics(out[rows], exact)
+    assert f["n_bad"] == 0, f
+    assert torch.equal(hidden[rows], ref_hidden), "updated residual is not bit-exact"
+    assert _lib_status_clear()
+    print(f"M={M} H={H} N={N} {dtype} sched={schedule}: {m} faithful={f}")
+    return m
+
+
+def _lib_status_clear() -> bool:
+    from triton_fused_rmsnorm_qkv import device_status
+    return device_status() == 0
+
+
+# ---------------------------------------------------------------- benchmark configs
+LLAMA8B = (4096, 6144)
+QWEN2 = (3584, 4608)
+LLAMA70B = (8192, 10240)
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 64])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+def test_llama3_8b_decode(M, dtype):
+    run_case(M, *LLAMA8B, dtype, seed=100 + M)
+
+
+@pytest.mark.parametrize("M", [1, 16, 64])
+@pytest.mark.parametrize("res", [False, True], ids=["R0", "R1"])
+def test_qwen2_7b_decode(M, res):
+    run_case(M, *QWEN2, torch.bfloat16, seed=200 + M, res=res, eps=1e-6)
+
+
+@pytest.mark.parametrize("M", [512, 2048, 8192])
+def test_llama3_8b_prefill(M):
+    run_case(M, *LLAMA8B, torch.bfloat16, seed=300 + M, sample_rows=96)
+
+
+@pytest.mark.parametrize("M", [1, 16, 256])
+def test_llama3_70b(M):
+    run_case(M, *LLAMA70B, torch.bfloat16, seed=400 + M, sample_rows=64)
+
+
+def test_cpu_ref_shape_on_gpu():
+    """configs[0]'s shape (4 tokens, H=256, N=512) in bf16 (the kernels take 16-bit data)."""
+    run_case(4, 256, 512, torch.bfloat16, seed=1)
+
+
+# ---------------------------------------------------------------- every schedule, edge shapes
+SCHEDULE_CASES = [
+    # M, H, N, schedules that can take it
+    (1, 512, 640, ("simt", "decode", "split", "prefill")),
+    (5, 264, 200, ("simt", "decode", "split", "prefill")),     # H % 64 != 0, ragged N
+    (16, 1024, 1280, ("simt", "decode", "split", "prefill")),
+    (33, 512, 768, ("simt", "decode", "split", "prefill")),
+    (64, 2048, 2560, ("simt", "decode", "split", "prefill")),
+    (100, 520, 392, ("simt", "split", "prefill")),
+    (128, 1024, 1536, ("simt", "split", "prefill")),
+    (129, 768, 1000, ("simt", "prefill")),
+    (777, 1024, 1280, ("simt", "prefill")),
+]
+
+
+@pytest.mark.parametrize("M,H,N,scheds", SCHEDULE_CASES, ids=[f"M{c[0]}_H{c[1]}_N{c[2]}" for c in SCHEDULE_CASES])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("res", [True, False], ids=["R1", "R0"])
+def test_every_schedule(M, H, N, scheds, dtype, res):
+    for s in scheds:
+        run_case(M, H, N, dtype, seed=M * 7 + H, res=res, schedule=s)
+
+
+@pytest.mark.parametrize("M,H", [(3, 100), (17, 250), (40, 4100)])
+def test_unaligned_hidden_runs_simt(M, H):
+    """H % 8 != 0 cannot use TMA: the automatic choice is the SIMT kernel."""
+    assert _lib.workspace_bytes(M, H, 300, _lib.BF16, _lib.SCHED_AUTO) == 0
+    run_case(M, H, 300, torch.bfloat16, seed=H)
+
+
+@pytest.mark.parametrize("gain_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_gain_dtypes(gain_dtype):
+    run_case(16, 1024, 1536, torch.bfloat16, seed=5, gain_dtype=gain_dtype)
+    run_case(300, 1024, 1536, torch.bfloat16, seed=6, gain_dtype=gain_dtype)
+
+
+@pytest.mark.parametrize("schedule", ["decode", "split", "prefill", "simt"])
+def test_strided_rows(schedule):
+    """x, residual and weight with row strides larger than their rows (views of wider
+    buffers), and an output slice check."""
+    M, H, N = 24, 1024, 1280
+    x, r, g, w = make_case(M, H, N, torch.bfloat16, 77)
+    dev = "cuda"
+    xb = torch.zeros(M, H + 64, dtype=x.dtype, device=dev)
+    rb = torch.zeros(M, H + 128, dtype=x.dtype, device=dev)
+    wb = torch.zeros(N, H + 32, dtype=x.dtype, device=dev)
+    xb[:, :H] = x.to(dev)
+    rb[:, :H] = r.to(dev)
+    wb[:, :H] = w.to(dev)
+    xv, rv, wv = xb[:, :H], rb[:, :H], wb[:, :H]
+    assert xv.stride(0) == H + 64 and wv.stride(0) == H + 32
+    out, hidden = fused_add_rmsnorm_matmul(xv[None], rv[None], g.to(dev), wv, 1e-5, schedule=schedule)
+    ref_out, ref_hidden = forward(x, r, g, w, 1e-5)
+    m = parity_metrics(out[0].cpu(), ref_out)
+    assert within_bars(m, MAX_ABS, REL_L2), m
+    assert torch.equal(hidden[0].cpu(), ref_hidden)
+
+
+def test_static_weights_prefetch_matches():
+    a = run_case(16, 4096, 6144, torch.bfloat16, seed=9, static_weights=True)
+    b = run_case(16, 4096, 6144, torch.bfloat16, seed=9, static_weights=False)
+    assert a == b
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 2048])
+def test_deterministic(M):
+    x, r, g, w = (t.cuda() if t is not None else None for t in make_case(M, 4096, 6144, torch.bfloat16, 3))
+    a = fused_rmsnorm_residual_matmul(x[None], r[None], g, w, 1e-5)
+    b = fused_rmsnorm_residual_matmul(x[None], r[None], g, w, 1e-5)
+    assert torch.equal(a, b)
+
+
+def test_cuda_graph_capture_and_replay():
+    """The op captures into a CUDA graph (no host sync, no allocation inside the library)
+    and replays with new inputs copied into the captured buffers."""
+    M, H, N = 16, 4096, 6144
+    x, r, g, w = (t.cuda() for t in make_case(M, H, N, torch.bfloat16, 21))
+    xs, rs = x.clone()[None], r.clone()[None]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fused_add_rmsnorm_matmul(xs, rs, g, w, 1e-5)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out, hidden = fused_add_rmsnorm_matmul(xs, rs, g, w, 1e-5)
+    x2, r2, _, _ = make_case(M, H, N, torch.bfloat16, 22)
+    xs.copy_(x2.cuda()[None])
+    rs.copy_(r2.cuda()[None])
+    graph.replay()
+    torch.cuda.synchronize()
+    ref_out, ref_hidden = forward(x2, r2, g.cpu(), w.cpu(), 1e-5)
+    m = parity_metrics(out[0].cpu(), ref_out)
+    assert within_bars(m, MAX_ABS, REL_L2), m
+    assert torch.equal(hidden[0].cpu(), ref_hidden)
+    del graph
+
+
+def test_no_residual_writes_x_as_hidden():
+    M, H, N = 8, 1024, 1536
+    x, _, g, w = make_case(M, H, N, torch.bfloat16, 31, has_residual=False)
+    out, hidden = fused_add_rmsnorm_matmul(x.cuda()[None], None, g.cuda(), w.cuda(), 1e-5)
+    assert torch.equal(hidden[0].cpu(), x)
+
+
+def test_errors_are_raised_not_launched():
+    x = torch.randn(1, 4, 256, device="cuda", dtype=torch.bfloat16)
+    g = torch.ones(256, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(512, 256, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(TypeError):
+        fused_rmsnorm_residual_matmul(x.float(), None, g, w.float())
+    with pytest.raises(ValueError):
+        fused_rmsnorm_residual_matmul(x, None, torch.ones(128, device="cuda"), w)
+    with pytest.raises(AssertionError):
+        fused_rmsnorm_residual_matmul(x, None, g, torch.randn(512, 128, device="cuda", dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        fused_rmsnorm_residual_matmul(x, None, g, w, residual_out=torch.empty(1, 4, 128, device="cuda",
+                                                                              dtype=torch.bfloat16))
+    with pytest.raises(ValueError):  # forced decode schedule beyond its 64-row limit
+        fused_rmsnorm_residual_matmul(torch.randn(1, 65, 256, device="cuda", dtype=torch.bfloat16), None, g, w,
+                                      schedule="decode")
+    with pytest.raises(ValueError):  # in-place residual update is rejected (residual_out aliases residual)
+        r = torch.randn_like(x)
+        fused_rmsnorm_residual_matmul(x, r, g, w, residual_out=r)

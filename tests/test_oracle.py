@@ -1,0 +1,81 @@
+"""The CPU oracle against the reference's own outputs (golden vectors) and the
+known-answer properties of the reference's tests.  CPU only."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from cases import CASES, as_bits, inputs_digest
+from oracle import forward, make_case, parity_metrics, rms_normalize, split_qkv
+
+GOLDEN = np.load(Path(__file__).resolve().parent / "golden" / "golden.npz")
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_oracle_matches_reference_golden(case):
+    """Bit-exact: the oracle reproduces the reference's baseline.py output and hidden."""
+    torch.set_num_threads(1)
+    x, r, g, w = make_case(case["M"], case["H"], case["N"], case["dtype"], case["seed"], case["res"])
+    assert inputs_digest(x, r, g, w) == str(GOLDEN[case["name"] + "__digest"]), \
+        "regenerated inputs differ from the ones the golden vectors were made from"
+    out, hidden = forward(x, r, g, w, case["eps"])
+    np.testing.assert_array_equal(as_bits(out), GOLDEN[case["name"] + "__out"])
+    np.testing.assert_array_equal(as_bits(hidden), GOLDEN[case["name"] + "__hidden"])
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c["dtype"] != torch.float32], ids=lambda c: c["name"])
+def test_fp32_accumulation_mode_within_tolerance(case):
+    """The fast fp32-accumulate projection stays within the parity bar of the native one."""
+    x, r, g, w = make_case(case["M"], case["H"], case["N"], case["dtype"], case["seed"], case["res"])
+    a, _ = forward(x, r, g, w, case["eps"], accumulate="native")
+    b, _ = forward(x, r, g, w, case["eps"], accumulate="fp32")
+    m = parity_metrics(b, a)
+    assert m["max_abs"] <= 2e-2 and m["rel_l2"] <= 5e-3, m
+
+
+def test_identity_projection_gives_equal_qkv():
+    """tests/test_correctness.py:142-155: identity weight, unit gain -> Q == K == V."""
+    torch.manual_seed(0)
+    H = 128
+    x = torch.randn(16, H)
+    g = torch.ones(H)
+    w = torch.eye(H).repeat(3, 1)
+    out, _ = forward(x, torch.zeros_like(x), g, w, 1e-6)
+    q, k, v = split_qkv(out, H, H)
+    torch.testing.assert_close(q, k, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(k, v, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(q, rms_normalize(x, g, 1e-6), atol=1e-5, rtol=1e-5)
+
+
+def test_zero_residual_has_no_nan():
+    """tests/test_correctness.py:127-140."""
+    x, _, _, w = make_case(128, 256, 768, torch.float16, 0)
+    out, hidden = forward(x, torch.zeros_like(x), torch.ones(256, dtype=torch.float16), w, 1e-6)
+    assert not torch.isnan(out).any()
+    assert torch.equal(hidden, x)
+
+
+def test_split_widths_gqa():
+    """integration/llama3_patch.py:156-158 and tests/test_correctness.py:327-346."""
+    H, H_kv = 512, 128
+    x, r, g, w = make_case(4, H, H + 2 * H_kv, torch.bfloat16, 9)
+    out, _ = forward(x, r, g, w, 1e-5)
+    q, k, v = split_qkv(out, H, H_kv)
+    assert q.shape == (4, H) and k.shape == (4, H_kv) and v.shape == (4, H_kv)
+
+
+def test_residual_add_is_fp32_add_rounded():
+    """hidden = RNE_dtype(fp32(x) + fp32(r)): the contract the kernels reproduce bit for bit."""
+    for dt in (torch.float16, torch.bfloat16):
+        x, r, _, _ = make_case(64, 512, 8, dt, 11)
+        hidden, _ = forward(x, r, torch.ones(512, dtype=dt), torch.zeros(8, 512, dtype=dt), 1e-5)[::-1]
+        assert torch.equal(hidden, (x.float() + r.float()).to(dt))
+
+
+def test_parity_metrics():
+    a = torch.tensor([1.0, 2.0, 3.0])
+    m = parity_metrics(a + torch.tensor([0.0, 0.01, 0.0]), a)
+    assert abs(m["max_abs"] - 0.01) < 1e-6 and m["nonfinite"] == 0
