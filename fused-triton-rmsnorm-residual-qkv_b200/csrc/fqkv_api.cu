@@ -373,7 +373,7 @@ extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const v
     if (int rc = make_map(&tmW, weight, N, H, ldw, 128, bf16)) return rc;
     if (int rc = make_map(&tmB, normed, M, H, H, c.mpad, bf16)) return rc;
     StreamKParams sp{static_cast<uint16_t*>(out), partials, counters, (int)M, (int)N, (int)H, ldo,
-                     (int)((H + 63) / 64), tiles128, flags};
+                     (int)((H + 63) / 64), tiles128, flags, c.b_slots, c.w_evict_first};
     // Chained to the pre-pass: the GEMM may start streaming the weight before the
     // pre-pass finishes only if the caller declared the weight static.
     e = launch_streamk(c, tmW, tmB, sp, bf16, true, st);

@@ -42,10 +42,11 @@ constexpr int kMaxCluster = 8;
 constexpr int kTileRows = 128;      // rows of W per MMA (UMMA M)
 constexpr int kKBlock = 64;         // K elements per stage (128 bytes of 16-bit data)
 constexpr int kWTileBytes = kTileRows * 128;
-constexpr int kLoadBatch = 8;       // 16-byte chunks per lane loaded before any is used
+constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
+constexpr int kGainChunks = 4;      // gain chunks per thread: K slices up to 4 * 128 * 8 elements
 
 struct Layout {
-  uint32_t ring, stage_bytes, normed, red, rowp, rstd, bars, tmem_slot, total;
+  uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, bars, tmem_slot, total;
 };
 
 __host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max) {
@@ -53,11 +54,12 @@ __host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int 
   L.stage_bytes = nt * kWTileBytes;
   L.ring = 0;
   L.normed = L.ring + stages * L.stage_bytes;
-  L.red = L.normed + (uint32_t)nkb_max * mpad * 128;  // [kMaxCluster][mpad] floats
+  L.gain = L.normed + (uint32_t)nkb_max * mpad * 128;  // [nkb_max * 64] fp32 gain slice
+  L.red = L.gain + (uint32_t)nkb_max * kKBlock * 4;    // [kMaxCluster][mpad] floats
   L.rowp = L.red + kMaxCluster * mpad * 4;            // [mpad] floats
   L.rstd = L.rowp + mpad * 4;                         // [mpad] floats
-  L.bars = (L.rstd + mpad * 4 + 7) & ~7u;             // full[S], empty[S], accum, normed, sum, part
-  L.tmem_slot = L.bars + (2 * stages + 4) * 8;
+  L.bars = (L.rstd + mpad * 4 + 7) & ~7u;             // full[S], empty[S], accum, normed, sum, part, acts
+  L.tmem_slot = L.bars + (2 * stages + 5) * 8;
   L.total = L.tmem_slot + 16;
   return L;
 }
@@ -83,6 +85,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* normed_bar = accum_bar + 1;
   uint64_t* sum_bar = accum_bar + 2;
   uint64_t* part_bar = accum_bar + 3;
+  uint64_t* acts_bar = accum_bar + 4;  // the norm warps have issued their activation loads
+  float* gain_s = reinterpret_cast<float*>(smem + L.gain);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   float* part = reinterpret_cast<float*>(ring);  // [NT][MPAD][128] partial tile, aliases the ring
 
@@ -105,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(normed_bar, 1);
     mbar_init(sum_bar, C * 32);
     mbar_init(part_bar, C * 128);
+    mbar_init(acts_bar, 1);
     fence_mbarrier_init_cluster();
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tmW);
@@ -123,12 +128,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t tx = L.stage_bytes;
       // The weight does not depend on the preceding grid when the caller says so: start
-      // streaming it before that grid has finished.
+      // streaming it before that grid has finished.  Only `pre` stages go out before the
+      // norm warps have requested their activations, so those small, latency-critical
+      // loads are not queued behind megabytes of weight in the memory system.
       if (!(p.flags & FQKV_FLAG_STATIC_WEIGHTS)) pdl_wait();
+      const int pre = min(nkb, min(stages, p.pre_stages));
       const uint64_t pol_w = policy_evict_first();
       bool ok = true;
       int s = 0, round = 0, issued = 0;
       for (int i = 0; i < nkb; ++i) {
+        if (i == pre) ok = mbar_wait(acts_bar, 0);
         if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
         mbar_arrive_expect_tx(&full[s], tx);
         tma_load_2d_hint(ring + s * L.stage_bytes, &tmW, &full[s], (kb0 + i) * kKBlock, n_base, pol_w);
@@ -176,48 +185,86 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ norm + epilogue (warps 2..5)
     const int et = threadIdx.x - 64;  // 0..127
     bool ok = true;
-    pdl_wait();
     const int nw = warp - 2;
     const int nchunk = nkb * 8;  // 16-byte chunks per row of the slice
     const int64_t k_lo = (int64_t)kb0 * kKBlock;
+    const bool static_w = (p.flags & FQKV_FLAG_STATIC_WEIGHTS) != 0;
     const bool write_res = p.rout != nullptr && blockIdx.y == 0;
-    // Pass 1: one warp per row; each lane issues kLoadBatch chunk loads of x (and r)
-    // before consuming any, so a row costs one memory latency per batch.
-    for (int m = nw; m < MPAD; m += 4) {
-      float ss = 0.f;
-      const bool live = m < p.M;
-      const uint16_t* xr = p.x + (int64_t)m * p.ldx;
-      const uint16_t* rr = p.r ? p.r + (int64_t)m * p.ldr : nullptr;
-      for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
-        uint4 xv[kLoadBatch], rv[kLoadBatch];
+    // The gain slice: loads go out now (into registers) and land in shared memory after
+    // pass 1, so their latency overlaps that of the activations.  It is a weight: with
+    // static weights it is read before the preceding grid has finished.
+    float4 gv[kGainChunks][2];
+    auto issue_gain = [&]() {
 #pragma unroll
-        for (int b = 0; b < kLoadBatch; ++b) {
-          const int j = j0 + lane + 32 * b;
-          const int64_t k = k_lo + (int64_t)j * 8;
-          xv[b] = make_uint4(0, 0, 0, 0);
-          rv[b] = make_uint4(0, 0, 0, 0);
-          if (live && j < nchunk && k < p.H) {
-            xv[b] = __ldg(reinterpret_cast<const uint4*>(xr + k));
-            if (rr) rv[b] = __ldg(reinterpret_cast<const uint4*>(rr + k));
+      for (int i = 0; i < kGainChunks; ++i) {
+        const int j = et + 128 * i;
+        const int64_t k = k_lo + (int64_t)j * 8;
+        gv[i][0] = gv[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < nchunk && k < p.H) load_gain8(p.g, p.gdt, k, gv[i]);
+      }
+    };
+    if (static_w) issue_gain();
+    pdl_wait();
+    if (!static_w) issue_gain();
+    // Pass 1: each warp takes rows nw, nw + 4, ... two at a time; each lane issues up to
+    // kLoadBatch chunk loads of x (and r) per row before consuming any, so a pair of rows
+    // costs one memory latency.
+    for (int m0 = nw; m0 < MPAD; m0 += 8) {
+      float ss[2] = {0.f, 0.f};
+      for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
+        uint4 xv[2][kLoadBatch], rv[2][kLoadBatch];
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int m = m0 + 4 * q2;
+          const bool live = m < p.M;
+          const uint16_t* xr = p.x + (int64_t)m * p.ldx;
+          const uint16_t* rr = p.r ? p.r + (int64_t)m * p.ldr : nullptr;
+#pragma unroll
+          for (int b = 0; b < kLoadBatch; ++b) {
+            const int j = j0 + lane + 32 * b;
+            const int64_t k = k_lo + (int64_t)j * 8;
+            xv[q2][b] = make_uint4(0, 0, 0, 0);
+            rv[q2][b] = make_uint4(0, 0, 0, 0);
+            if (live && j < nchunk && k < p.H) {
+              xv[q2][b] = __ldg(reinterpret_cast<const uint4*>(xr + k));
+              if (rr) rv[q2][b] = __ldg(reinterpret_cast<const uint4*>(rr + k));
+            }
           }
         }
+        if (m0 == nw && j0 == 0 && et == 0) mbar_arrive(acts_bar);  // the first loads are out
 #pragma unroll
-        for (int b = 0; b < kLoadBatch; ++b) {
-          const int j = j0 + lane + 32 * b;
-          if (j >= nchunk) continue;
-          const int64_t k = k_lo + (int64_t)j * 8;
-          uint4 hv = xv[b];
-          if (live && k < p.H) {
-            if (rr) hv = add_rne8<T>(hv, rv[b]);
-            ss = sumsq8_acc<T>(hv, ss);
-            if (write_res) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int m = m0 + 4 * q2;
+          const bool live = m < p.M;
+#pragma unroll
+          for (int b = 0; b < kLoadBatch; ++b) {
+            const int j = j0 + lane + 32 * b;
+            if (j >= nchunk) continue;
+            const int64_t k = k_lo + (int64_t)j * 8;
+            uint4 hv = xv[q2][b];
+            if (live && k < p.H) {
+              if (p.r) hv = add_rne8<T>(hv, rv[q2][b]);
+              ss[q2] = sumsq8_acc<T>(hv, ss[q2]);
+              if (write_res) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
+            }
+            *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
           }
-          *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
         }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) rowp[m] = ss;
+      for (int q2 = 0; q2 < 2; ++q2) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss[q2] += __shfl_xor_sync(0xffffffffu, ss[q2], o);
+        if (lane == 0) rowp[m0 + 4 * q2] = ss[q2];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kGainChunks; ++i) {
+      const int j = et + 128 * i;
+      if (j < nchunk) {
+        reinterpret_cast<float4*>(gain_s)[2 * j] = gv[i][0];
+        reinterpret_cast<float4*>(gain_s)[2 * j + 1] = gv[i][1];
+      }
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");
     // Publish this CTA's per-row partial sums into slot `rank` of every CTA.
@@ -241,8 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t k = k_lo + (int64_t)j * 8;
       if (m >= p.M || k >= p.H) continue;
       uint4* ptr = reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
-      float4 gv[2];
-      load_gain8(p.g, p.gdt, k, gv);
+      const float4 gv[2] = {reinterpret_cast<const float4*>(gain_s)[2 * j], reinterpret_cast<const float4*>(gain_s)[2 * j + 1]};
       *ptr = normalize8g<T>(*ptr, rstd_s[m], gv);
     }
     fence_proxy_async_smem();
@@ -394,6 +440,7 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
     const int tiles = (N + nt * kTileRows - 1) / (nt * kTileRows);
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
+      if ((KB + cl - 1) / cl * 8 > kGainChunks * 128) continue;  // gain slice held in registers
       // The epilogue's partial tile aliases the ring.
       const int min_stages = (nt * mpad * kTileRows * 4 + nt * kWTileBytes - 1) / (nt * kWTileBytes);
       for (int st = 16; st >= max(2, min_stages); --st) {
@@ -434,7 +481,9 @@ cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const D
     ++na;
   }
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, k, tmW, p, c.stages);
+  DecodeParams q = p;
+  q.pre_stages = env_int("FQKV_DECODE_PRE", 2);
+  return cudaLaunchKernelEx(&cfg, k, tmW, q, c.stages);
 }
 
 }  // namespace fqkv

@@ -49,6 +49,7 @@ struct DecodeParams {
   int kb_total;       // ceil(H / 64)
   int nkb_max;        // max k-blocks of one CTA's K slice
   int flags;
+  int pre_stages;     // weight stages issued before the activation loads are out
 };
 
 struct StreamKParams {
@@ -60,6 +61,8 @@ struct StreamKParams {
   int kb_total;
   int tiles;
   int flags;
+  int b_slots;        // > 0: normalised rows resident in shared memory (slots of MPAD x 64)
+  int w_evict_first;  // weight loads carry an L2 evict-first hint
 };
 
 struct GemmParams {
@@ -178,11 +181,13 @@ size_t decode_smem_bytes(const DecodeConfig& c, int kb_total);
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream);
 
-constexpr int kStreamKMaxGrid = 160;  // partial-slot capacity of the workspace (>= SM count)
+constexpr int kStreamKMaxGrid = 320;  // partial-slot capacity of the workspace (>= 2 x SM count)
 struct StreamKConfig {
   int mpad;
   int stages;
   int grid;
+  int b_slots;
+  int w_evict_first;
   size_t smem;
 };
 int streamk_mpad(int M);

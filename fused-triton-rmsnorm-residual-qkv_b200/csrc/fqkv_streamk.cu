@@ -33,14 +33,17 @@ constexpr int kKBlock = 64;
 constexpr int kWTileBytes = kTileRows * 128;
 
 struct SLayout {
-  uint32_t stage_bytes, bars, flag, tmem_slot, total;
+  uint32_t stage_bytes, bres, bars, flag, tmem_slot, total;
 };
 
-__host__ __device__ inline SLayout make_slayout(int stages, int mpad) {
+// b_slots > 0: the normalised rows of the CTA's k-blocks stay resident (b_slots tiles of
+// MPAD x 64, loaded once); 0: each stage carries its own MPAD x 64 tile next to the weight.
+__host__ __device__ inline SLayout make_slayout(int stages, int mpad, int b_slots) {
   SLayout L;
-  L.stage_bytes = kWTileBytes + mpad * 128;
-  L.bars = stages * L.stage_bytes;  // full[S], empty[S], tfull[2], tempty[2], done
-  L.flag = L.bars + (2 * stages + 5) * 8;
+  L.stage_bytes = kWTileBytes + (b_slots > 0 ? 0 : mpad * 128);
+  L.bres = stages * L.stage_bytes;
+  L.bars = L.bres + b_slots * mpad * 128;  // full[S], empty[S], tfull[2], tempty[2], done, bfull
+  L.flag = L.bars + (2 * stages + 6) * 8;
   L.tmem_slot = L.flag + 8;
   L.total = L.tmem_slot + 16;
   return L;
@@ -63,12 +66,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const StreamKParams p, const int stages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SLayout L = make_slayout(stages, MPAD);
+  const SLayout L = make_slayout(stages, MPAD, p.b_slots);
+  const bool bres = p.b_slots > 0;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + 2;
   uint64_t* done_bar = tempty + 2;
+  uint64_t* bfull = tempty + 3;
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L.flag);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   constexpr uint32_t kTmemCols = 2 * MPAD <= 32 ? 32u : 2 * MPAD <= 64 ? 64u : 2 * MPAD <= 128 ? 128u : 256u;
@@ -88,12 +93,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[b], 128);
     }
     mbar_init(done_bar, 1);
+    mbar_init(bfull, 1);
     fence_mbarrier_init_cluster();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmB);
   }
+  // k-blocks this CTA touches: a range of n_b (mod KB) starting at kb_s; the resident copy
+  // of k-block kb lives in slot (kb - kb_s) mod KB.
+  const int kb_s = (int)(u0 % KB);
+  const int n_b = (int)((u1 - u0) < (int64_t)KB ? (u1 - u0) : (int64_t)KB);
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -110,27 +120,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tx = L.stage_bytes;
       const int n_units = (int)(u1 - u0);
       const int pre = (p.flags & FQKV_FLAG_STATIC_WEIGHTS) ? min(stages, n_units) : 0;
+      const bool hint = p.w_evict_first != 0;
       const uint64_t pol_w = policy_evict_first();
+      auto load_w = [&](int slot, int64_t u) {
+        void* dst = smem + slot * L.stage_bytes;
+        const int kx = (int)(u % KB) * kKBlock, ky = (int)(u / KB) * kTileRows;
+        if (hint) tma_load_2d_hint(dst, &tmW, &full[slot], kx, ky, pol_w);
+        else tma_load_2d(dst, &tmW, &full[slot], kx, ky);
+      };
       // The weight does not depend on the preceding grid when the caller says so: start
       // streaming it before the pre-pass has finished.
       for (int i = 0; i < pre; ++i) {
-        const int64_t u = u0 + i;
         mbar_arrive_expect_tx(&full[i], tx);
-        tma_load_2d_hint(smem + i * L.stage_bytes, &tmW, &full[i], (int)(u % KB) * kKBlock,
-                         (int)(u / KB) * kTileRows, pol_w);
+        load_w(i, u0 + i);
       }
       pdl_wait();  // normalised rows come from the pre-pass
-      for (int i = 0; i < pre; ++i)
-        tma_load_2d(smem + i * L.stage_bytes + kWTileBytes, &tmB, &full[i], (int)((u0 + i) % KB) * kKBlock, 0);
+      if (bres) {
+        mbar_arrive_expect_tx(bfull, (uint32_t)(n_b * MPAD * 128));
+        for (int j = 0; j < n_b; ++j)
+          tma_load_2d(smem + L.bres + j * (MPAD * 128), &tmB, bfull, ((kb_s + j) % KB) * kKBlock, 0);
+      } else {
+        for (int i = 0; i < pre; ++i)
+          tma_load_2d(smem + i * L.stage_bytes + kWTileBytes, &tmB, &full[i], (int)((u0 + i) % KB) * kKBlock, 0);
+      }
       bool ok = true;
       int s = pre % stages, round = pre / stages, issued = pre;
       for (int64_t u = u0 + pre; u < u1; ++u) {
         if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
         mbar_arrive_expect_tx(&full[s], tx);
-        uint8_t* st = smem + s * L.stage_bytes;
-        const int kx = (int)(u % KB) * kKBlock;
-        tma_load_2d_hint(st, &tmW, &full[s], kx, (int)(u / KB) * kTileRows, pol_w);
-        tma_load_2d(st + kWTileBytes, &tmB, &full[s], kx, 0);
+        load_w(s, u);
+        if (!bres) tma_load_2d(smem + s * L.stage_bytes + kWTileBytes, &tmB, &full[s], (int)(u % KB) * kKBlock, 0);
         ++issued;
         if (++s == stages) {
           s = 0;
@@ -138,13 +157,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       for (int j = max(0, issued - stages); j < issued; ++j) mbar_wait(&full[j % stages], (j / stages) & 1);
+      if (bres) mbar_wait(bfull, 0);
       (void)ok;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(kTileRows, MPAD, std::is_same<T, __nv_bfloat16>::value);
-      bool ok = true;
+      bool ok = !bres || mbar_wait(bfull, 0);
       int s = 0, round = 0, seg = 0;
       bool first = true;
       uint32_t d_tmem = tmem_base;
@@ -160,7 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(&full[s], round & 1))) break;
         tc_fence_after();
         const uint32_t a_base = smem_u32(smem + s * L.stage_bytes);
-        const uint32_t b_base = a_base + kWTileBytes;
+        const uint32_t b_base =
+            bres ? smem_u32(smem + L.bres + (((kb - kb_s + KB) % KB) * (MPAD * 128))) : a_base + kWTileBytes;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_f16(d_tmem, make_sw128_desc(a_base + kk * 32), make_sw128_desc(b_base + kk * 32), idesc,
@@ -320,23 +341,36 @@ int streamk_mpad(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 12
 int64_t streamk_partials_bytes(int M) { return (int64_t)kStreamKMaxGrid * 2 * streamk_mpad(M) * kTileRows * 4; }
 int64_t streamk_counters_bytes(int N) { return (int64_t)((N + kTileRows - 1) / kTileRows) * 4; }
 
+static int env_or(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+// Grid: every SM (FQKV_SPLIT_CTAS_PER_SM CTAs each, default 1), at most one CTA per unit.
+// The normalised rows stay resident when the CTA's k-blocks fit in kBResidentMax bytes.
+// Ring: as deep as fits in the per-CTA share of shared memory (FQKV_SPLIT_STAGES overrides).
 int streamk_pick_config(int M, int H, int N, int sm_count, StreamKConfig* cfg) {
   StreamKConfig c{};
   c.mpad = streamk_mpad(M);
   if (M > 128) return FQKV_ERR_SCHEDULE;
-  const int64_t units = (int64_t)((N + kTileRows - 1) / kTileRows) * ((H + kKBlock - 1) / kKBlock);
-  int g = sm_count < kStreamKMaxGrid ? sm_count : kStreamKMaxGrid;
-  if (units < g) g = (int)units;
-  c.grid = g;
-  // Ring depth: as deep as fits while two CTAs share an SM, so the next launch (PDL) can
-  // start streaming its weight while this one drains.  FQKV_SPLIT_STAGES overrides.
-  const char* env = std::getenv("FQKV_SPLIT_STAGES");
-  const size_t limit = kSmemLimitSK / 2 - 1024;
+  const int KB = (H + kKBlock - 1) / kKBlock;
+  const int64_t units = (int64_t)((N + kTileRows - 1) / kTileRows) * KB;
+  const int per_sm = max(1, min(2, env_or("FQKV_SPLIT_CTAS_PER_SM", 1)));
+  int64_t g = (int64_t)sm_count * per_sm;
+  if (g > kStreamKMaxGrid) g = kStreamKMaxGrid;
+  if (units < g) g = units;
+  c.grid = (int)g;
+  const int64_t max_units = (units + g - 1) / g;
+  const int b_slots = (int)(max_units < (int64_t)KB ? max_units : (int64_t)KB);
+  const int bres_max = env_or("FQKV_SPLIT_BRES_MAX", 48 * 1024);
+  c.b_slots = (int64_t)b_slots * c.mpad * 128 <= bres_max ? b_slots : 0;
+  const size_t limit = kSmemLimitSK / per_sm - 1024;
   c.stages = 2;
-  while (c.stages < 16 && 1024 + make_slayout(c.stages + 1, c.mpad).total <= limit) ++c.stages;
-  if (env && *env) c.stages = std::atoi(env);
-  if (c.stages < 2 || 1024 + make_slayout(c.stages, c.mpad).total > kSmemLimitSK) return FQKV_ERR_SCHEDULE;
-  c.smem = 1024 + make_slayout(c.stages, c.mpad).total;
+  while (c.stages < 16 && 1024 + make_slayout(c.stages + 1, c.mpad, c.b_slots).total <= limit) ++c.stages;
+  c.stages = env_or("FQKV_SPLIT_STAGES", c.stages);
+  c.w_evict_first = env_or("FQKV_W_EVICT_FIRST", 1);
+  if (c.stages < 2 || 1024 + make_slayout(c.stages, c.mpad, c.b_slots).total > kSmemLimitSK) return FQKV_ERR_SCHEDULE;
+  c.smem = 1024 + make_slayout(c.stages, c.mpad, c.b_slots).total;
   *cfg = c;
   return 0;
 }

@@ -96,10 +96,10 @@ def test_python_error_mapping():
 
 
 def _split_bytes(M, H, N):
-    """Normalised rows + stream-K partial slots (160 CTAs x 2 x MPAD x 128 fp32) + counters."""
+    """Normalised rows + stream-K partial slots (320 CTAs x 2 x MPAD x 128 fp32) + counters."""
     a = lambda b: (b + 255) // 256 * 256  # noqa: E731
     mpad = 16 if M <= 16 else 32 if M <= 32 else 64 if M <= 64 else 128
-    return a(M * H * 2) + a(160 * 2 * mpad * 128 * 4) + a(((N + 127) // 128) * 4)
+    return a(M * H * 2) + a(320 * 2 * mpad * 128 * 4) + a(((N + 127) // 128) * 4)
 
 
 @pytest.mark.parametrize("M,H,sched,expect", [
