@@ -1,0 +1,144 @@
+"""Route each Llama decoder layer's input RMSNorm + Q/K/V projections through the fused op.
+
+Same public surface and behaviour as the reference's ``integration/llama3_patch.py``:
+
+* ``apply_fused_patch(model)`` stores, per ``LlamaDecoderLayer``, the packed GQA weight
+  ``[Wq; Wk; Wv]`` of shape ``(H + 2 * H_kv, H)`` (no zero padding, llama3_patch.py:111-127)
+  and rebinds the layer's ``forward`` (llama3_patch.py:206-215);
+* the patched forward calls ``fused_rmsnorm_residual_matmul(hidden_states, None,
+  input_layernorm.weight, packed, eps)`` -- Llama adds its residual after attention, so
+  the fused call has none (llama3_patch.py:148-154) -- then splits Q/K/V by their real
+  widths and runs the unchanged rest of the layer (RoPE, KV cache, attention, o_proj,
+  residual, post-attention norm, MLP, residual; llama3_patch.py:156-196);
+* ``TRITON_FUSED_DISABLE_AUTOTUNE=1`` selects the ``_fixed`` entry point
+  (llama3_patch.py:61-65);
+* ``remove_fused_patch`` / ``fused_patch`` undo it (llama3_patch.py:218-239).
+
+Written against transformers 5.5 (``LlamaDecoderLayer.forward`` / ``LlamaAttention``).
+"""
+from __future__ import annotations
+
+import os
+from contextlib import contextmanager
+from typing import Optional
+
+import torch
+from transformers import LlamaConfig, LlamaForCausalLM
+from transformers.models.llama.modeling_llama import (
+    ALL_ATTENTION_FUNCTIONS,
+    LlamaAttention,
+    apply_rotary_pos_emb,
+    eager_attention_forward,
+)
+
+from triton_fused_rmsnorm_qkv import fused_rmsnorm_residual_matmul, fused_rmsnorm_residual_matmul_fixed
+
+LLAMA3_8B_CONFIG = dict(
+    hidden_size=4096,
+    intermediate_size=14336,
+    num_hidden_layers=32,
+    num_attention_heads=32,
+    num_key_value_heads=8,
+    head_dim=128,
+    max_position_embeddings=8192,
+    rms_norm_eps=1e-5,
+    vocab_size=128256,
+    rope_theta=500000.0,
+    tie_word_embeddings=False,
+    attention_bias=False,
+    mlp_bias=False,
+)
+
+_ORIGINAL = "_fused_original_forward"
+
+
+def _fused_op():
+    """The fused entry point for this call (env TRITON_FUSED_DISABLE_AUTOTUNE=1 -> _fixed)."""
+    if os.environ.get("TRITON_FUSED_DISABLE_AUTOTUNE") == "1":
+        return fused_rmsnorm_residual_matmul_fixed
+    return fused_rmsnorm_residual_matmul
+
+
+def build_llama3_8b(dtype: torch.dtype = torch.float16, device: str = "cuda",
+                    num_hidden_layers: Optional[int] = None) -> LlamaForCausalLM:
+    """A Llama-3-8B-shaped ``LlamaForCausalLM`` with random weights, in eval mode."""
+    cfg = dict(LLAMA3_8B_CONFIG)
+    if num_hidden_layers is not None:
+        cfg["num_hidden_layers"] = num_hidden_layers
+    saved = torch.get_default_dtype()
+    torch.set_default_dtype(dtype)
+    try:
+        with torch.device(device):
+            model = LlamaForCausalLM(LlamaConfig(**cfg))
+    finally:
+        torch.set_default_dtype(saved)
+    return model.eval()
+
+
+def pack_qkv_weight(attn: LlamaAttention) -> torch.Tensor:
+    """``[Wq; Wk; Wv]`` stacked along the output dimension, without padding."""
+    wq, wk, wv = attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight
+    hidden = wq.shape[1]
+    if wq.shape[0] != hidden:
+        raise ValueError(f"q_proj must map {hidden} -> {hidden}, got {tuple(wq.shape)}")
+    if wk.shape != wv.shape:
+        raise ValueError(f"k_proj {tuple(wk.shape)} and v_proj {tuple(wv.shape)} must have the same shape")
+    return torch.cat([wq.detach(), wk.detach(), wv.detach()], dim=0).contiguous()
+
+
+def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
+                     use_cache=False, position_embeddings=None, **kwargs):
+    """LlamaDecoderLayer.forward with input_layernorm + q/k/v_proj replaced by one fused op."""
+    attn = self.self_attn
+    lead = hidden_states.shape[:-1]
+    h_kv = self._fused_H_kv
+    h_q = self._fused_packed_qkv.shape[0] - 2 * h_kv
+    qkv = _fused_op()(hidden_states, None, self.input_layernorm.weight, self._fused_packed_qkv,
+                      eps=self.input_layernorm.variance_epsilon)
+    q, k, v = torch.split(qkv, [h_q, h_kv, h_kv], dim=-1)
+    q = q.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
+    k = k.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
+    v = v.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
+    cos, sin = position_embeddings
+    q, k = apply_rotary_pos_emb(q, k, cos, sin)
+    if past_key_values is not None:
+        k, v = past_key_values.update(k, v, attn.layer_idx)
+    attend = ALL_ATTENTION_FUNCTIONS.get_interface(attn.config._attn_implementation, eager_attention_forward)
+    ctx, _ = attend(attn, q, k, v, attention_mask, dropout=0.0, scaling=attn.scaling, **kwargs)
+    hidden_states = hidden_states + attn.o_proj(ctx.reshape(*lead, -1).contiguous())
+    return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
+
+
+def apply_fused_patch(model: LlamaForCausalLM) -> LlamaForCausalLM:
+    """Patch every decoder layer of ``model`` (idempotent)."""
+    for layer in model.model.layers:
+        if hasattr(layer, _ORIGINAL):
+            continue
+        layer._fused_packed_qkv = pack_qkv_weight(layer.self_attn)
+        layer._fused_H_kv = layer.self_attn.k_proj.weight.shape[0]
+        setattr(layer, _ORIGINAL, layer.forward)
+        layer.forward = _patched_forward.__get__(layer, type(layer))
+    return model
+
+
+def remove_fused_patch(model: LlamaForCausalLM) -> LlamaForCausalLM:
+    """Restore the original forward of every patched layer and drop the packed weights."""
+    for layer in model.model.layers:
+        if not hasattr(layer, _ORIGINAL):
+            continue
+        layer.forward = getattr(layer, _ORIGINAL)
+        delattr(layer, _ORIGINAL)
+        for name in ("_fused_packed_qkv", "_fused_H_kv"):
+            if hasattr(layer, name):
+                delattr(layer, name)
+    return model
+
+
+@contextmanager
+def fused_patch(model: LlamaForCausalLM):
+    """Apply the patch for the duration of a ``with`` block."""
+    apply_fused_patch(model)
+    try:
+        yield model
+    finally:
+        remove_fused_patch(model)

@@ -1,0 +1,88 @@
+"""The Llama-3 integration: packing and patch bookkeeping on the CPU, end-to-end logits
+of a patched model against the unpatched one on the GPU."""
+from __future__ import annotations
+
+import pytest
+import torch
+from transformers import LlamaConfig, LlamaForCausalLM
+
+from integration import LLAMA3_8B_CONFIG, apply_fused_patch, build_llama3_8b, fused_patch, remove_fused_patch
+from integration.llama3_patch import pack_qkv_weight
+
+
+def tiny_llama(device="cpu", dtype=torch.float32, layers=2):
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=layers, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=64, vocab_size=500, max_position_embeddings=128,
+                      rms_norm_eps=1e-5, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    saved = torch.get_default_dtype()
+    torch.set_default_dtype(dtype)
+    try:
+        with torch.device(device):
+            return LlamaForCausalLM(cfg).eval()
+    finally:
+        torch.set_default_dtype(saved)
+
+
+def test_pack_is_q_then_k_then_v_without_padding():
+    model = tiny_llama()
+    attn = model.model.layers[0].self_attn
+    packed = pack_qkv_weight(attn)
+    assert packed.shape == (256 + 2 * 128, 256)
+    assert torch.equal(packed[:256], attn.q_proj.weight)
+    assert torch.equal(packed[256:384], attn.k_proj.weight)
+    assert torch.equal(packed[384:], attn.v_proj.weight)
+
+
+def test_patch_and_unpatch_bookkeeping():
+    model = tiny_llama()
+    originals = [layer.forward for layer in model.model.layers]
+    apply_fused_patch(model)
+    apply_fused_patch(model)  # idempotent
+    for layer in model.model.layers:
+        assert hasattr(layer, "_fused_packed_qkv") and layer._fused_H_kv == 128
+    remove_fused_patch(model)
+    for layer, fwd in zip(model.model.layers, originals):
+        assert not hasattr(layer, "_fused_packed_qkv")
+        assert layer.forward == fwd
+    with fused_patch(model):
+        assert all(hasattr(layer, "_fused_packed_qkv") for layer in model.model.layers)
+    assert not any(hasattr(layer, "_fused_packed_qkv") for layer in model.model.layers)
+
+
+def test_llama3_8b_config_shape():
+    assert LLAMA3_8B_CONFIG["hidden_size"] + 2 * LLAMA3_8B_CONFIG["num_key_value_heads"] * \
+        LLAMA3_8B_CONFIG["head_dim"] == 6144
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fixed", [False, True], ids=["auto", "fixed"])
+def test_patched_tiny_llama_matches_unpatched(fixed, monkeypatch):
+    if fixed:
+        monkeypatch.setenv("TRITON_FUSED_DISABLE_AUTOTUNE", "1")
+    model = tiny_llama("cuda", torch.bfloat16)
+    ids = torch.randint(0, 500, (2, 24), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    with torch.no_grad():
+        ref = model(ids).logits.float()
+        with fused_patch(model):
+            got = model(ids).logits.float()
+    rel = (got - ref).norm() / ref.norm()
+    assert rel < 2e-2, float(rel)
+
+
+@pytest.mark.gpu
+def test_patched_llama3_8b_two_layers_decode_and_prefill():
+    """The Llama-3-8B layer shape (2 layers): prefill of 32 tokens, then 4 greedy decode
+    steps through the KV cache, patched vs unpatched."""
+    model = build_llama3_8b(dtype=torch.bfloat16, device="cuda", num_hidden_layers=2)
+    ids = torch.randint(0, 128256, (1, 32), device="cuda", generator=torch.Generator(device="cuda").manual_seed(2))
+    with torch.no_grad():
+        ref = model.generate(ids, max_new_tokens=4, do_sample=False, output_logits=True, return_dict_in_generate=True)
+        with fused_patch(model):
+            got = model.generate(ids, max_new_tokens=4, do_sample=False, output_logits=True,
+                                 return_dict_in_generate=True)
+    for a, b in zip(got.logits, ref.logits):
+        rel = (a.float() - b.float()).norm() / b.float().norm()
+        assert rel < 3e-2, float(rel)
+    del model
+    torch.cuda.empty_cache()
