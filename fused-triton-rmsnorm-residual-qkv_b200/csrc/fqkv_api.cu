@@ -390,3 +390,105 @@ extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const v
   e = launch_gemm(g, tmA, tmB, gp, bf16, true, st);
   return e == cudaSuccess ? 0 : cuda_fail(e, "prefill GEMM launch");
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory when they run the op: an inference
+// engine's plugin whose enqueue step must not allocate (the engine owns all memory and
+// forbids the implicit device synchronisation cudaMalloc can cause), a runtime with a
+// fixed memory budget that allocates nothing after start-up, or code running while a
+// stream is being captured.  They cannot hand fqkv_launch the workspace its pre-pass
+// schedule needs, so fqkv_launch_noalloc runs that schedule (norm pre-pass + stream-K
+// GEMM) on a fixed array of device memory that belongs to the library.
+//
+// The array is a file-scope __device__ variable: every GPU that loads the library holds
+// its own copy (kNoAllocScratchBytes, about 5.5 MB) until the process exits.  Its
+// device address is looked up with cudaGetSymbolAddress the first time the entry point
+// runs on a device (with that device current); make that first call before capturing a
+// stream.  All calls on a device share the array and it keeps the last call's contents:
+// the pre-pass zeroes the arrival counters each call, the other regions are fully
+// rewritten before they are read.  Calls whose kernels overlap on the GPU (e.g. issued
+// on two streams at once) race on the array and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace fqkv {
+namespace {
+
+constexpr int64_t kNoAllocMaxM = 16;
+constexpr int64_t kNoAllocMaxH = 8192;
+constexpr int64_t kNoAllocMaxN = 16384;
+constexpr size_t kNoAllocNormedBytes = (size_t)kNoAllocMaxM * kNoAllocMaxH * 2;           // 256 KiB
+constexpr size_t kNoAllocPartialBytes = (size_t)kStreamKMaxGrid * 2 * 16 * 128 * 4;       // 5 MiB (MPAD 16)
+constexpr size_t kNoAllocCounterBytes = (size_t)((kNoAllocMaxN + 127) / 128) * 4;         // 512 B
+constexpr size_t kNoAllocScratchBytes = kNoAllocNormedBytes + kNoAllocPartialBytes + kNoAllocCounterBytes;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of this device's copy of g_noalloc_scratch (looked up once per device).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FQKV_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+}  // namespace fqkv
+
+extern "C" FQKV_API int fqkv_launch_noalloc(const void* x, const void* residual, const void* rms_weight,
+                                            int rms_weight_dtype, const void* weight, void* out, void* residual_out,
+                                            int64_t M, int64_t H, int64_t N, int64_t ldx, int64_t ldr, int64_t ldw,
+                                            int64_t ldo, int64_t ldro, float eps, int dtype, int flags,
+                                            void* stream) {
+  Problem p{M, H, N, ldx, ldr, ldw, ldo, ldro, x, residual, rms_weight, weight, out, residual_out,
+            dtype, rms_weight_dtype, FQKV_SCHED_SPLIT, flags};
+  if (int rc = validate(p)) return rc;
+  if (M > kNoAllocMaxM || H > kNoAllocMaxH || N > kNoAllocMaxN)
+    return fail(FQKV_ERR_SHAPE,
+                "fqkv_launch_noalloc takes M <= %lld, H <= %lld, N <= %lld (its scratch is a fixed %zu-byte "
+                "device array); got M=%lld H=%lld N=%lld -- use fqkv_launch with a workspace",
+                (long long)kNoAllocMaxM, (long long)kNoAllocMaxH, (long long)kNoAllocMaxN, kNoAllocScratchBytes,
+                (long long)M, (long long)H, (long long)N);
+  DeviceInfo d;
+  if (int rc = device_info(&d)) return rc;
+  if (d.major != 10) return fail(FQKV_ERR_DEVICE, "compute capability %d.%d is not sm_100", d.major, d.minor);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  uint16_t* normed = reinterpret_cast<uint16_t*>(base);
+  float* partials = reinterpret_cast<float*>(base + kNoAllocNormedBytes);
+  int* counters = reinterpret_cast<int*>(base + kNoAllocNormedBytes + kNoAllocPartialBytes);
+  const int tiles128 = (int)((N + 127) / 128);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = dtype == FQKV_BF16;
+
+  StreamKConfig c;
+  if (int rc = streamk_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
+  if (c.mpad != 16) return fail(FQKV_ERR_SHAPE, "internal: unexpected tile width %d", c.mpad);
+  CUtensorMap tmW, tmB;
+  if (int rc = make_map(&tmW, weight, N, H, ldw, 128, bf16)) return rc;
+  if (int rc = make_map(&tmB, normed, M, H, H, c.mpad, bf16)) return rc;
+
+  PrepassParams pp{static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(residual), rms_weight,
+                   rms_weight_dtype, static_cast<uint16_t*>(residual_out), normed, M, H, ldx, ldr, ldro, eps,
+                   counters, tiles128};
+  cudaError_t e = launch_prepass(pp, bf16, (flags & FQKV_FLAG_PDL) != 0, st);
+  if (e != cudaSuccess) return cuda_fail(e, "norm pre-pass launch");
+  StreamKParams sp{static_cast<uint16_t*>(out), partials, counters, (int)M, (int)N, (int)H, ldo,
+                   (int)((H + 63) / 64), tiles128, flags, c.b_slots, c.w_evict_first};
+  e = launch_streamk(c, tmW, tmB, sp, bf16, true, st);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "stream-K GEMM launch");
+}

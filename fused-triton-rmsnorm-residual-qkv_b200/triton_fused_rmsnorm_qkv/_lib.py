@@ -31,6 +31,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libfqkv.so"
 
 EXPORTED_SYMBOLS = (
     "fqkv_launch",
+    "fqkv_launch_noalloc",
     "fqkv_workspace_bytes",
     "fqkv_query_schedule",
     "fqkv_last_error",

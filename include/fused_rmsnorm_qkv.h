@@ -132,6 +132,26 @@ FQKV_API const char* fqkv_last_error(void);
  * current device.  *status receives FQKV_STATUS_* bits. */
 FQKV_API int fqkv_device_status(void* stream, int* status);
 
+/*
+ * The op without a workspace, for callers that cannot allocate device memory when they
+ * run it -- an inference engine's plugin whose enqueue step must not allocate, a runtime
+ * with a fixed memory budget, code running while a stream is being captured.  No
+ * counterpart in the reference (its Triton kernels need no scratch).
+ * Runs the SPLIT schedule (norm pre-pass + stream-K GEMM) on a fixed device array owned
+ * by the library (about 5.5 MB on every GPU that loads the library, held until exit), so
+ * it takes M <= 16, H <= 8192 and N <= 16384; larger problems return FQKV_ERR_SHAPE.
+ * Arguments are those of fqkv_launch minus schedule and workspace.  The first call on a
+ * device looks up the array's address (cudaGetSymbolAddress) and should come before any
+ * stream capture.  All calls on a device share the array: calls whose kernels overlap on
+ * the GPU (e.g. on two streams at once) race and must be serialised by the caller.
+ * Allocates nothing.
+ */
+FQKV_API int fqkv_launch_noalloc(const void* x, const void* residual, const void* rms_weight,
+                int rms_weight_dtype, const void* weight, void* out, void* residual_out,
+                int64_t M, int64_t H, int64_t N,
+                int64_t ldx, int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro,
+                float eps, int dtype, int flags, void* stream);
+
 /* ABI version (major * 100 + minor). */
 FQKV_API int fqkv_version(void);
 
