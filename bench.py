@@ -509,10 +509,14 @@ def main() -> int:
     ap.add_argument("--no-detail", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--sets", type=int, default=None,
+                    help="rotating weight sets (default: the workload's; fewer only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.sets:
+        wl["sets"] = args.sets
     M = args.m or wl["M"]
     world, rank, _ = dist_env()
     if args.impl == "reference":

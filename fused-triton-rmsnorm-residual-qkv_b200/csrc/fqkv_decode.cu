@@ -37,13 +37,15 @@
 namespace fqkv {
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kNormWarps = 8;                  // warps 2 .. 9: norm, then epilogue
+constexpr int kNormThreads = kNormWarps * 32;
+constexpr int kThreads = 64 + kNormThreads;
 constexpr int kMaxCluster = 8;
 constexpr int kTileRows = 128;      // rows of W per MMA (UMMA M)
 constexpr int kKBlock = 64;         // K elements per stage (128 bytes of 16-bit data)
 constexpr int kWTileBytes = kTileRows * 128;
 constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
-constexpr int kGainChunks = 4;      // gain chunks per thread: K slices up to 4 * 128 * 8 elements
+constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
 
 struct Layout {
   uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, bars, tmem_slot, total;
@@ -107,8 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(accum_bar, 1);
     mbar_init(normed_bar, 1);
-    mbar_init(sum_bar, C * 32);
-    mbar_init(part_bar, C * 128);
+    mbar_init(sum_bar, 1);      // local arrive + C * MPAD * 4 bytes of st.async from the cluster
+    mbar_init(part_bar, C);     // one (relaxed, fenced) arrive per CTA of the cluster
     mbar_init(acts_bar, 1);
     fence_mbarrier_init_cluster();
   }
@@ -182,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(accum_bar, 0);  // all MMAs retired before TMEM is freed
     }
   } else {
-    // ------------------------------------------------------------ norm + epilogue (warps 2..5)
-    const int et = threadIdx.x - 64;  // 0..127
+    // ------------------------------------------------------------ norm + epilogue (warps 2..9)
+    const int et = threadIdx.x - 64;  // 0 .. kNormThreads - 1
     bool ok = true;
     const int nw = warp - 2;
     const int nchunk = nkb * 8;  // 16-byte chunks per row of the slice
@@ -193,29 +195,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The gain slice: loads go out now (into registers) and land in shared memory after
     // pass 1, so their latency overlaps that of the activations.  It is a weight: with
     // static weights it is read before the preceding grid has finished.
-    float4 gv[kGainChunks][2];
+    uint4 graw[kGainChunks][2];
     auto issue_gain = [&]() {
 #pragma unroll
       for (int i = 0; i < kGainChunks; ++i) {
-        const int j = et + 128 * i;
+        const int j = et + kNormThreads * i;
         const int64_t k = k_lo + (int64_t)j * 8;
-        gv[i][0] = gv[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < nchunk && k < p.H) load_gain8(p.g, p.gdt, k, gv[i]);
+        graw[i][0] = graw[i][1] = make_uint4(0, 0, 0, 0);
+        if (j < nchunk && k < p.H) load_gain8_raw(p.g, p.gdt, k, graw[i]);
       }
     };
+    // This CTA expects C * MPAD row sums (4 bytes each) from the cluster's st.async writes.
+    if (et == 0) mbar_arrive_expect_tx_cluster(sum_bar, C * MPAD * 4);
     if (static_w) issue_gain();
     pdl_wait();
     if (!static_w) issue_gain();
-    // Pass 1: each warp takes rows nw, nw + 4, ... two at a time; each lane issues up to
-    // kLoadBatch chunk loads of x (and r) per row before consuming any, so a pair of rows
-    // costs one memory latency.
-    for (int m0 = nw; m0 < MPAD; m0 += 8) {
+    // Pass 1: warp nw takes rows nw, nw + 8, nw + 16, ... two at a time; each lane issues
+    // up to kLoadBatch chunk loads of x (and r) per row before consuming any, so a pair of
+    // rows costs one memory latency (M = 16: one pair per warp).
+    for (int m0 = nw; m0 < MPAD; m0 += 2 * kNormWarps) {
       float ss[2] = {0.f, 0.f};
       for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
         uint4 xv[2][kLoadBatch], rv[2][kLoadBatch];
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
-          const int m = m0 + 4 * q2;
+          const int m = m0 + kNormWarps * q2;
           const bool live = m < p.M;
           const uint16_t* xr = p.x + (int64_t)m * p.ldx;
           const uint16_t* rr = p.r ? p.r + (int64_t)m * p.ldr : nullptr;
@@ -231,10 +235,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (m0 == nw && j0 == 0 && et == 0) mbar_arrive(acts_bar);  // the first loads are out
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
-          const int m = m0 + 4 * q2;
+          const int m = m0 + kNormWarps * q2;
           const bool live = m < p.M;
 #pragma unroll
           for (int b = 0; b < kLoadBatch; ++b) {
@@ -255,55 +258,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int q2 = 0; q2 < 2; ++q2) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss[q2] += __shfl_xor_sync(0xffffffffu, ss[q2], o);
-        if (lane == 0) rowp[m0 + 4 * q2] = ss[q2];
+        if (lane == 0) rowp[m0 + kNormWarps * q2] = ss[q2];
       }
     }
 #pragma unroll
     for (int i = 0; i < kGainChunks; ++i) {
-      const int j = et + 128 * i;
+      const int j = et + kNormThreads * i;
       if (j < nchunk) {
-        reinterpret_cast<float4*>(gain_s)[2 * j] = gv[i][0];
-        reinterpret_cast<float4*>(gain_s)[2 * j + 1] = gv[i][1];
+        float4 gv[2];
+        gain_raw_to_f32(p.gdt, graw[i], gv);
+        reinterpret_cast<float4*>(gain_s)[2 * j] = gv[0];
+        reinterpret_cast<float4*>(gain_s)[2 * j + 1] = gv[1];
       }
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    // Publish this CTA's per-row partial sums into slot `rank` of every CTA.
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    // Every activation load has returned: the producer may now fill the whole ring.
+    if (et == 0) mbar_arrive(acts_bar);
+    // Publish this CTA's per-row partial sums into slot `rank` of every CTA: each st.async
+    // counts its 4 bytes on the receiving CTA's sum_bar.
     if (warp == 2) {
       for (uint32_t c = 0; c < C; ++c) {
+        const uint32_t bar_c = mapa_shared(smem_u32(sum_bar), c);
         for (int m = lane; m < MPAD; m += 32)
-          st_cluster_f32(mapa_shared(smem_u32(&red[rank * MPAD + m]), c), rowp[m]);
-        mbar_arrive_remote(mapa_shared(smem_u32(sum_bar), c));
+          st_async_f32(mapa_shared(smem_u32(&red[rank * MPAD + m]), c), rowp[m], bar_c);
       }
     }
     ok = mbar_wait<true>(sum_bar, 0);
-    for (int m = et; m < MPAD; m += 128) {
+    for (int m = et; m < MPAD; m += kNormThreads) {
       float tot = 0.f;
       for (uint32_t c = 0; c < C; ++c) tot += red[c * MPAD + m];
       rstd_s[m] = row_rstd(tot, p.H, p.eps);
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    // Pass 2: normalise in place, dtype((h * rstd) * g).
-    for (int idx = et; idx < MPAD * nchunk; idx += 128) {
-      const int m = idx / nchunk, j = idx - m * nchunk;
-      const int64_t k = k_lo + (int64_t)j * 8;
-      if (m >= p.M || k >= p.H) continue;
-      uint4* ptr = reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
-      const float4 gv[2] = {reinterpret_cast<const float4*>(gain_s)[2 * j], reinterpret_cast<const float4*>(gain_s)[2 * j + 1]};
-      *ptr = normalize8g<T>(*ptr, rstd_s[m], gv);
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    // Pass 2: normalise in place, dtype((h * rstd) * g), with pass 1's warp/row mapping;
+    // each lane's kLoadBatch chunks of a row are independent (loads issued together).
+    for (int m = nw; m < p.M; m += kNormWarps) {
+      const float rs = rstd_s[m];
+      for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
+        uint4 hv[kLoadBatch];
+        float4 gv[kLoadBatch][2];
+#pragma unroll
+        for (int b = 0; b < kLoadBatch; ++b) {
+          const int j = j0 + lane + 32 * b;
+          if (j < nchunk && k_lo + (int64_t)j * 8 < p.H) {
+            hv[b] = *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
+            gv[b][0] = reinterpret_cast<const float4*>(gain_s)[2 * j];
+            gv[b][1] = reinterpret_cast<const float4*>(gain_s)[2 * j + 1];
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kLoadBatch; ++b) {
+          const int j = j0 + lane + 32 * b;
+          if (j < nchunk && k_lo + (int64_t)j * 8 < p.H)
+            *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) =
+                normalize8g<T>(hv[b], rs, gv[b]);
+        }
+      }
     }
     fence_proxy_async_smem();
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, 256;" ::: "memory");
     if (et == 0) mbar_arrive(normed_bar);
 
     // Epilogue: TMEM -> registers -> this CTA's partial tile in shared memory.
     ok = mbar_wait(accum_bar, 0) && ok;
     tc_fence_after();
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;             // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;   // the two warps of a quadrant split the 16-column chunks
     const int row = q * 32 + lane;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int c0 = 0; c0 < MPAD; c0 += 16) {
+        if (((nt * (MPAD / 16) + c0 / 16) & 1) != half) continue;
         uint32_t v[16];
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + nt * MPAD + c0, v);
         tmem_wait_ld();
@@ -312,13 +338,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     tc_fence_before();
-    for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote(mapa_shared(smem_u32(part_bar), c));
+    // One release per CTA: the CTA barrier orders every thread's partial-tile writes before
+    // thread 0's cluster fence, which the relaxed remote arrives then publish.
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (et == 0) {
+      fence_acq_rel_cluster();
+      for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
+    }
     ok = mbar_wait<true>(part_bar, 0) && ok;
     // Reduce 1/C of the tile across the cluster (fixed order over ranks) and store it.
     const int64_t total = (int64_t)NT * p.M * kTileRows;
     const int64_t f0 = (rank * total) / C, f1 = ((rank + 1) * total) / C;
     const uint32_t part_base = smem_u32(part);
-    for (int64_t f = f0 + et; f < f1; f += 128) {
+    for (int64_t f = f0 + et; f < f1; f += kNormThreads) {
       const int nl = (int)(f % kTileRows);
       const int64_t rest = f / kTileRows;
       const int nt = (int)(rest % NT);
@@ -440,7 +472,7 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
     const int tiles = (N + nt * kTileRows - 1) / (nt * kTileRows);
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
-      if ((KB + cl - 1) / cl * 8 > kGainChunks * 128) continue;  // gain slice held in registers
+      if ((KB + cl - 1) / cl * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
       // The epilogue's partial tile aliases the ring.
       const int min_stages = (nt * mpad * kTileRows * 4 + nt * kWTileBytes - 1) / (nt * kWTileBytes);
       for (int st = 16; st >= max(2, min_stages); --st) {

@@ -68,6 +68,29 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Relaxed remote arrive: pair with one fence_acq_rel_cluster() before a batch of them.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+
+// Local arrive that also announces `bytes` of incoming transactions (cluster scope: the
+// bytes come from st.async writes of other CTAs).
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.relaxed.cluster.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Store 4 bytes into another CTA's shared memory and count them on that CTA's mbarrier
+// (complete_tx); the data is visible to whoever observes the barrier phase complete.
+__device__ __forceinline__ void st_async_f32(uint32_t cluster_addr, float v, uint32_t cluster_bar) {
+  asm volatile("st.async.weak.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(cluster_addr),
+               "r"(__float_as_uint(v)), "r"(cluster_bar)
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -295,11 +318,20 @@ struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ uint16_t from_f(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
   }
+  // Two values rounded to nearest-even and packed (low half = a): one cvt instruction.
+  static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
 };
 template <>
 struct Elem<__half> {
   static __device__ __forceinline__ float to_f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
   static __device__ __forceinline__ uint16_t from_f(float f) { return __half_as_ushort(__float2half_rn(f)); }
+  static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
 };
 
 // Gain element k as fp32 (the gain may be fp32, fp16 or bf16, kernel.py:203).

@@ -84,8 +84,8 @@ __device__ __forceinline__ uint16_t add_rne1(uint16_t a, uint16_t b) {
 
 template <typename T>
 __device__ __forceinline__ uint32_t add_rne2(uint32_t a, uint32_t b) {
-  return (uint32_t)add_rne1<T>((uint16_t)(a & 0xFFFFu), (uint16_t)(b & 0xFFFFu)) |
-         ((uint32_t)add_rne1<T>((uint16_t)(a >> 16), (uint16_t)(b >> 16)) << 16);
+  return Elem<T>::from_f2(__fadd_rn(Elem<T>::to_f((uint16_t)(a & 0xFFFFu)), Elem<T>::to_f((uint16_t)(b & 0xFFFFu))),
+                          __fadd_rn(Elem<T>::to_f((uint16_t)(a >> 16)), Elem<T>::to_f((uint16_t)(b >> 16))));
 }
 
 template <typename T>
@@ -148,6 +148,39 @@ __device__ __forceinline__ void load_gain8(const void* g, int gdt, int64_t k, fl
   out[1] = make_float4(f[4], f[5], f[6], f[7]);
 }
 
+// The 16 bytes (bf16/fp16) or 32 bytes (fp32) of gain elements k .. k+7, raw; converted
+// later by gain_raw_to_f32 so that issuing the loads never waits for them.
+__device__ __forceinline__ void load_gain8_raw(const void* g, int gdt, int64_t k, uint4 (&raw)[2]) {
+  if (gdt == FQKV_F32) {
+    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(g) + k);
+    raw[0] = __ldg(p);
+    raw[1] = __ldg(p + 1);
+  } else {
+    raw[0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(g) + k));
+    raw[1] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ void gain_raw_to_f32(int gdt, const uint4 (&raw)[2], float4 (&out)[2]) {
+  if (gdt == FQKV_F32) {
+    out[0] = make_float4(__uint_as_float(raw[0].x), __uint_as_float(raw[0].y), __uint_as_float(raw[0].z),
+                         __uint_as_float(raw[0].w));
+    out[1] = make_float4(__uint_as_float(raw[1].x), __uint_as_float(raw[1].y), __uint_as_float(raw[1].z),
+                         __uint_as_float(raw[1].w));
+    return;
+  }
+  const uint32_t w[4] = {raw[0].x, raw[0].y, raw[0].z, raw[0].w};
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint16_t lo = (uint16_t)(w[i] & 0xFFFFu), hi = (uint16_t)(w[i] >> 16);
+    f[2 * i] = gdt == FQKV_BF16 ? Elem<__nv_bfloat16>::to_f(lo) : Elem<__half>::to_f(lo);
+    f[2 * i + 1] = gdt == FQKV_BF16 ? Elem<__nv_bfloat16>::to_f(hi) : Elem<__half>::to_f(hi);
+  }
+  out[0] = make_float4(f[0], f[1], f[2], f[3]);
+  out[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
 // normalize8 with the gain already in registers.
 template <typename T>
 __device__ __forceinline__ uint4 normalize8g(uint4 h, float rstd, const float4 (&g)[2]) {
@@ -156,9 +189,9 @@ __device__ __forceinline__ uint4 normalize8g(uint4 h, float rstd, const float4 (
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint16_t lo = normalize1<T>((uint16_t)(w[i] & 0xFFFFu), rstd, gf[2 * i]);
-    const uint16_t hi = normalize1<T>((uint16_t)(w[i] >> 16), rstd, gf[2 * i + 1]);
-    o[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+    const float lo = __fmul_rn(__fmul_rn(Elem<T>::to_f((uint16_t)(w[i] & 0xFFFFu)), rstd), gf[2 * i]);
+    const float hi = __fmul_rn(__fmul_rn(Elem<T>::to_f((uint16_t)(w[i] >> 16)), rstd), gf[2 * i + 1]);
+    o[i] = Elem<T>::from_f2(lo, hi);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }

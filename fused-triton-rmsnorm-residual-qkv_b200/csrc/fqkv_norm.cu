@@ -16,11 +16,12 @@ namespace fqkv {
 
 // ---------------------------------------------------------------------------
 // Pre-pass: one CTA (256 threads) per row; requires H % 8 == 0, H <= 16384 and
-// 16-byte aligned rows.  Each thread keeps up to 8 chunks of 8 elements in registers.
+// 16-byte aligned rows.  Each thread keeps CPT chunks of 8 elements in registers
+// (CPT = ceil(H / 2048), so the register footprint, and hence occupancy, follows H).
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, int CPT>
 __global__ void __launch_bounds__(256) norm_prepass_kernel(const PrepassParams p) {
-  constexpr int kMaxChunks = 8;
+  constexpr int kMaxChunks = CPT;
   __shared__ float warp_sums[8];
   pdl_launch_dependents();
   pdl_wait();
@@ -163,8 +164,18 @@ cudaError_t launch_prepass(const PrepassParams& p, bool bf16, bool pdl, cudaStre
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return bf16 ? cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__nv_bfloat16>, p)
-              : cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__half>, p);
+  const int64_t cpt = (p.H / 8 + 255) / 256;
+  if (cpt <= 1)
+    return bf16 ? cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__nv_bfloat16, 1>, p)
+                : cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__half, 1>, p);
+  if (cpt <= 2)
+    return bf16 ? cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__nv_bfloat16, 2>, p)
+                : cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__half, 2>, p);
+  if (cpt <= 4)
+    return bf16 ? cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__nv_bfloat16, 4>, p)
+                : cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__half, 4>, p);
+  return bf16 ? cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__nv_bfloat16, 8>, p)
+              : cudaLaunchKernelEx(&cfg, norm_prepass_kernel<__half, 8>, p);
 }
 
 cudaError_t launch_simt(const SimtParams& p, bool bf16, bool pdl, cudaStream_t stream) {
