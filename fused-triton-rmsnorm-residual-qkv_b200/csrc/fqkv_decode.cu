@@ -19,9 +19,9 @@
 //              exchange per-row partial sums of squares across the cluster through
 //              DSMEM, then normalise in place: dtype((h * rstd) * g) (baseline.py:59-62).
 //              The normalised activations never leave shared memory.
-//              Epilogue: TMEM -> registers -> shared memory; the C partial sums of a
-//              tile are reduced through DSMEM in a fixed order (deterministic) and
-//              each CTA stores 1/C of the tile.
+//              Epilogue: TMEM -> registers -> shared memory; each CTA reduces 1/C of
+//              the tile over the cluster's C partial tiles (16-byte DSMEM loads, fixed
+//              rank order: deterministic) and stores it.
 // The host sizes (NT, C, STAGES) so that all clusters are resident at once
 // (cudaOccupancyMaxActiveClusters): a second wave would double the time.
 // Every wait is bounded (fqkv_device.cuh); after a timeout the kernel drains its own
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accum_bar = empty + stages;
   uint64_t* normed_bar = accum_bar + 1;
   uint64_t* sum_bar = accum_bar + 2;
-  uint64_t* part_bar = accum_bar + 3;
+  uint64_t* part_bar = accum_bar + 3;  // every CTA of the cluster has written its partial tile
   uint64_t* acts_bar = accum_bar + 4;  // the norm warps have issued their activation loads
   float* gain_s = reinterpret_cast<float*>(smem + L.gain);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // up to kLoadBatch chunk loads of x (and r) per row before consuming any, so a pair of
     // rows costs one memory latency (M = 16: one pair per warp).
     for (int m0 = nw; m0 < MPAD; m0 += 2 * kNormWarps) {
-      float ss[2] = {0.f, 0.f};
+      uint64_t ss2[2] = {0ull, 0ull};  // fp32 pairs: even / odd elements
       for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
         uint4 xv[2][kLoadBatch], rv[2][kLoadBatch];
 #pragma unroll
@@ -246,8 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t k = k_lo + (int64_t)j * 8;
             uint4 hv = xv[q2][b];
             if (live && k < p.H) {
-              if (p.r) hv = add_rne8<T>(hv, rv[q2][b]);
-              ss[q2] = sumsq8_acc<T>(hv, ss[q2]);
+              if (p.r) hv = add8_rn<T>(hv, rv[q2][b]);
+              ss2[q2] = sumsq8_f2<T>(hv, ss2[q2]);
               if (write_res) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
             }
             *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
@@ -256,9 +256,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int q2 = 0; q2 < 2; ++q2) {
+        float lo, hi;
+        f2_unpack(ss2[q2], lo, hi);
+        float ss = lo + hi;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss[q2] += __shfl_xor_sync(0xffffffffu, ss[q2], o);
-        if (lane == 0) rowp[m0 + kNormWarps * q2] = ss[q2];
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) rowp[m0 + kNormWarps * q2] = ss;
       }
     }
 #pragma unroll
@@ -290,28 +293,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       rstd_s[m] = row_rstd(tot, p.H, p.eps);
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    // Pass 2: normalise in place, dtype((h * rstd) * g), with pass 1's warp/row mapping;
-    // each lane's kLoadBatch chunks of a row are independent (loads issued together).
-    for (int m = nw; m < p.M; m += kNormWarps) {
-      const float rs = rstd_s[m];
-      for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
+    // Pass 2: normalise in place, dtype((h * rstd) * g).  Warp nw takes pass 1's rows; a
+    // lane's gain pairs for its kLoadBatch chunks are loaded once and serve all its rows.
+    for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
+      uint64_t g2[kLoadBatch][4];
+#pragma unroll
+      for (int b = 0; b < kLoadBatch; ++b) {
+        const int j = j0 + lane + 32 * b;
+        if (j < nchunk) {
+          const ulonglong2 a = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j];
+          const ulonglong2 c = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j + 1];
+          g2[b][0] = a.x;
+          g2[b][1] = a.y;
+          g2[b][2] = c.x;
+          g2[b][3] = c.y;
+        }
+      }
+      for (int m = nw; m < p.M; m += kNormWarps) {
+        const float rs = rstd_s[m];
+        const uint64_t rs2 = f2_pack(rs, rs);
         uint4 hv[kLoadBatch];
-        float4 gv[kLoadBatch][2];
 #pragma unroll
         for (int b = 0; b < kLoadBatch; ++b) {
           const int j = j0 + lane + 32 * b;
-          if (j < nchunk && k_lo + (int64_t)j * 8 < p.H) {
+          if (j < nchunk && k_lo + (int64_t)j * 8 < p.H)
             hv[b] = *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
-            gv[b][0] = reinterpret_cast<const float4*>(gain_s)[2 * j];
-            gv[b][1] = reinterpret_cast<const float4*>(gain_s)[2 * j + 1];
-          }
         }
 #pragma unroll
         for (int b = 0; b < kLoadBatch; ++b) {
           const int j = j0 + lane + 32 * b;
           if (j < nchunk && k_lo + (int64_t)j * 8 < p.H)
             *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) =
-                normalize8g<T>(hv[b], rs, gv[b]);
+                normalize8_f2<T>(hv[b], rs2, g2[b]);
         }
       }
     }
@@ -346,34 +359,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
     }
     ok = mbar_wait<true>(part_bar, 0) && ok;
-    // Reduce 1/C of the tile across the cluster (fixed order over ranks) and store it.
-    const int64_t total = (int64_t)NT * p.M * kTileRows;
-    const int64_t f0 = (rank * total) / C, f1 = ((rank + 1) * total) / C;
+    // Reduce 1/C of the tile across the cluster and store it.  A step covers 4 consecutive
+    // output features: one 16-byte DSMEM load per rank, all C issued before the sum, which
+    // runs in rank order (deterministic).
+    const int64_t total4 = (int64_t)NT * p.M * (kTileRows / 4);
+    const int64_t f0 = (rank * total4) / C, f1 = ((rank + 1) * total4) / C;
     const uint32_t part_base = smem_u32(part);
+    const bool vec_store = (p.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 7) == 0;
     for (int64_t f = f0 + et; f < f1; f += kNormThreads) {
-      const int nl = (int)(f % kTileRows);
-      const int64_t rest = f / kTileRows;
+      const int nl = (int)(f % (kTileRows / 4)) * 4;
+      const int64_t rest = f / (kTileRows / 4);
       const int nt = (int)(rest % NT);
       const int m = (int)(rest / NT);
-      const int n = n_base + nt * kTileRows + nl;
       const uint32_t off = (uint32_t)(((nt * MPAD + m) * kTileRows + nl) * 4);
-      // All C peer loads are issued before the (fixed-order) sum.
-      float v[kMaxCluster];
+      float4 v[kMaxCluster];
 #pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c) v[c] = (uint32_t)c < C ? ld_cluster_f32(mapa_shared(part_base + off, c)) : 0.f;
-      float acc = 0.f;
+      for (int c = 0; c < kMaxCluster; ++c)
+        v[c] = (uint32_t)c < C ? ld_cluster_f32x4(mapa_shared(part_base + off, c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c) acc += v[c];
-      if (n < p.N) p.out[(int64_t)m * p.ldo + n] = Elem<T>::from_f(acc);
+      for (int c = 0; c < kMaxCluster; ++c) {
+        acc.x += v[c].x;
+        acc.y += v[c].y;
+        acc.z += v[c].z;
+        acc.w += v[c].w;
+      }
+      const int n = n_base + nt * kTileRows + nl;
+      uint16_t* dst = p.out + (int64_t)m * p.ldo + n;
+      if (vec_store && n + 3 < p.N) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(Elem<T>::from_f2(acc.x, acc.y), Elem<T>::from_f2(acc.z, acc.w));
+      } else {
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (n + e < p.N) dst[e] = Elem<T>::from_f(a4[e]);
+      }
     }
+    // This thread's last access to a peer's shared memory.
+    cluster_arrive_release_thread();
     (void)ok;
   }
 
   // ---------------------------------------------------------------- teardown
-  __syncwarp();
-  tc_fence_before();
-  cluster_sync();  // no CTA leaves while a peer may still read its shared memory
+  if (warp < 2) {
+    __syncwarp();
+    tc_fence_before();
+    cluster_arrive_release_thread();
+  }
+  // No CTA leaves while a peer may still read its shared memory.
+  cluster_wait_acquire_thread();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }

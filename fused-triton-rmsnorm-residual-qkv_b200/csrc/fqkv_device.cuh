@@ -175,6 +175,15 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// Untiled bulk copy global -> CTA-local shared memory (no multicast).  Both addresses
+// 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -210,6 +219,14 @@ __device__ __forceinline__ void cluster_sync() {
   cluster_arrive_release();
   cluster_wait_acquire();
 }
+// Per-thread (not warp-aligned) halves of the cluster barrier, for warps whose lanes
+// reach them at different points.
+__device__ __forceinline__ void cluster_arrive_release_thread() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire_thread() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
 
 // Shared::cluster address of the variable at `local_addr` in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
@@ -227,6 +244,16 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
 __device__ __forceinline__ float ld_cluster_f32(uint32_t cluster_addr) {
   float v;
   asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
+// 16-byte load (address 16-byte aligned) from the shared memory of a CTA of the cluster.
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t cluster_addr) {
+  float4 v;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "r"(cluster_addr)
+      : "memory");
   return v;
 }
 

@@ -93,6 +93,96 @@ __device__ __forceinline__ uint4 add_rne8(uint4 a, uint4 b) {
   return make_uint4(add_rne2<T>(a.x, b.x), add_rne2<T>(a.y, b.y), add_rne2<T>(a.z, b.z), add_rne2<T>(a.w, b.w));
 }
 
+// ------------------------------------------------------------------ packed fp32x2
+// Two fp32 values in one 64-bit register (element k in the low half, k + 1 in the high
+// half) for sm_100's fp32x2 instructions: one instruction, two IEEE round-to-nearest
+// results, so the values are those of the scalar __fmul_rn / __fmaf_rn.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// The two 16-bit elements of a 32-bit word as an fp32 pair.
+template <typename T>
+__device__ __forceinline__ uint64_t f2_from_word(uint32_t w);
+template <>
+__device__ __forceinline__ uint64_t f2_from_word<__nv_bfloat16>(uint32_t w) {
+  return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+template <>
+__device__ __forceinline__ uint64_t f2_from_word<__half>(uint32_t w) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return f2_pack(f.x, f.y);
+}
+
+// dtype(x + r) on two elements at once.  A 16-bit add rounded once to nearest even gives
+// the same bits as rounding the fp32 sum to the 16-bit type (what add_rne1 computes): the
+// fp32 sum of two bf16 values is exact unless their exponents differ by more than 16,
+// and of two fp16 values unless they differ by more than 13.  In those cases the smaller
+// operand is below 1/8 ulp of the larger, the exact sum is far from a rounding tie, and
+// both roundings return the same value.
+template <typename T>
+__device__ __forceinline__ uint32_t add2_rn(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t add2_rn<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <>
+__device__ __forceinline__ uint32_t add2_rn<__half>(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 add8_rn(uint4 a, uint4 b) {
+  return make_uint4(add2_rn<T>(a.x, b.x), add2_rn<T>(a.y, b.y), add2_rn<T>(a.z, b.z), add2_rn<T>(a.w, b.w));
+}
+
+// acc (an fp32 pair) + squares of the 8 elements: even elements in the low half, odd
+// in the high half, fused multiply-adds in element order.
+template <typename T>
+__device__ __forceinline__ uint64_t sumsq8_f2(uint4 v, uint64_t acc) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t e = f2_from_word<T>(w[i]);
+    acc = f2_fma(e, e, acc);
+  }
+  return acc;
+}
+
+// dtype((fp32(h) * rstd) * g) on 8 elements; rs2 = {rstd, rstd}, g2[i] = gain pair of
+// elements 2i, 2i + 1.  Same roundings, in the same order, as normalize1.
+template <typename T>
+__device__ __forceinline__ uint4 normalize8_f2(uint4 h, uint64_t rs2, const uint64_t (&g2)[4]) {
+  const uint32_t w[4] = {h.x, h.y, h.z, h.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float lo, hi;
+    f2_unpack(f2_mul(f2_mul(f2_from_word<T>(w[i]), rs2), g2[i]), lo, hi);
+    o[i] = Elem<T>::from_f2(lo, hi);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // ss + sum of squares of the 8 elements, in element order.
 template <typename T>
 __device__ __forceinline__ float sumsq8_acc(uint4 v, float ss) {
