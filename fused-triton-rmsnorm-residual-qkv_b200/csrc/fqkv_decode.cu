@@ -212,7 +212,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!static_w) issue_gain();
     // Pass 1: warp nw takes rows nw, nw + 8, nw + 16, ... two at a time; each lane issues
     // up to kLoadBatch chunk loads of x (and r) per row before consuming any, so a pair of
-    // rows costs one memory latency (M = 16: one pair per warp).
+    // rows costs one memory latency (M = 16: one pair per warp).  When that is all of the
+    // warp's work (MPAD = 16 and at most 32 * kLoadBatch chunks per row), h also stays in
+    // registers for pass 2.
+    const bool h_in_regs = MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
+    uint4 hkeep[2][kLoadBatch];
     for (int m0 = nw; m0 < MPAD; m0 += 2 * kNormWarps) {
       uint64_t ss2[2] = {0ull, 0ull};  // fp32 pairs: even / odd elements
       for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
@@ -239,18 +243,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q2 = 0; q2 < 2; ++q2) {
           const int m = m0 + kNormWarps * q2;
           const bool live = m < p.M;
+          // Branch-free over the batch (predicated stores only), so the chunks interleave:
+          // x and r are zero where a chunk is out of range, so h is zero and adds nothing.
 #pragma unroll
           for (int b = 0; b < kLoadBatch; ++b) {
             const int j = j0 + lane + 32 * b;
-            if (j >= nchunk) continue;
             const int64_t k = k_lo + (int64_t)j * 8;
-            uint4 hv = xv[q2][b];
-            if (live && k < p.H) {
-              if (p.r) hv = add8_rn<T>(hv, rv[q2][b]);
-              ss2[q2] = sumsq8_f2<T>(hv, ss2[q2]);
-              if (write_res) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
-            }
-            *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
+            const uint4 hv = p.r ? add8_rn<T>(xv[q2][b], rv[q2][b]) : xv[q2][b];
+            ss2[q2] = sumsq8_f2<T>(hv, ss2[q2]);
+            if (write_res && live && j < nchunk && k < p.H)
+              *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
+            hkeep[q2][b] = hv;
+            if (j < nchunk) *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
           }
         }
       }
@@ -293,38 +297,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       rstd_s[m] = row_rstd(tot, p.H, p.eps);
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    // Pass 2: normalise in place, dtype((h * rstd) * g).  Warp nw takes pass 1's rows; a
-    // lane's gain pairs for its kLoadBatch chunks are loaded once and serve all its rows.
-    for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
-      uint64_t g2[kLoadBatch][4];
+    // Pass 2: normalise, dtype((h * rstd) * g), over pass 1's rows and chunks; a lane's gain
+    // pairs for its kLoadBatch chunks are loaded once and serve all its rows.
+    auto load_g2 = [&](int j, uint64_t (&g2)[4]) {
+      const ulonglong2 a = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j];
+      const ulonglong2 c = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j + 1];
+      g2[0] = a.x;
+      g2[1] = a.y;
+      g2[2] = c.x;
+      g2[3] = c.y;
+    };
+    if (h_in_regs) {
+      uint64_t rs2[2];
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const float rs = rstd_s[nw + kNormWarps * q2];
+        rs2[q2] = f2_pack(rs, rs);
+      }
 #pragma unroll
       for (int b = 0; b < kLoadBatch; ++b) {
-        const int j = j0 + lane + 32 * b;
-        if (j < nchunk) {
-          const ulonglong2 a = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j];
-          const ulonglong2 c = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j + 1];
-          g2[b][0] = a.x;
-          g2[b][1] = a.y;
-          g2[b][2] = c.x;
-          g2[b][3] = c.y;
+        const int j = lane + 32 * b;
+        const bool in = j < nchunk && k_lo + (int64_t)j * 8 < p.H;
+        uint64_t g2[4];
+        load_g2(j < nchunk ? j : nchunk - 1, g2);  // clamped: always inside the gain slice
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int m = nw + kNormWarps * q2;
+          const uint4 o = normalize8_f2<T>(hkeep[q2][b], rs2[q2], g2);
+          if (in && m < p.M) *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = o;
         }
       }
-      for (int m = nw; m < p.M; m += kNormWarps) {
-        const float rs = rstd_s[m];
-        const uint64_t rs2 = f2_pack(rs, rs);
-        uint4 hv[kLoadBatch];
+    } else {
+      for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
+        uint64_t g2[kLoadBatch][4];
 #pragma unroll
         for (int b = 0; b < kLoadBatch; ++b) {
           const int j = j0 + lane + 32 * b;
-          if (j < nchunk && k_lo + (int64_t)j * 8 < p.H)
-            hv[b] = *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
+          if (j < nchunk) load_g2(j, g2[b]);
         }
+        for (int m = nw; m < p.M; m += kNormWarps) {
+          const float rs = rstd_s[m];
+          const uint64_t rs2 = f2_pack(rs, rs);
+          uint4 hv[kLoadBatch];
 #pragma unroll
-        for (int b = 0; b < kLoadBatch; ++b) {
-          const int j = j0 + lane + 32 * b;
-          if (j < nchunk && k_lo + (int64_t)j * 8 < p.H)
-            *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) =
-                normalize8_f2<T>(hv[b], rs2, g2[b]);
+          for (int b = 0; b < kLoadBatch; ++b) {
+            const int j = j0 + lane + 32 * b;
+            if (j < nchunk && k_lo + (int64_t)j * 8 < p.H)
+              hv[b] = *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
+          }
+#pragma unroll
+          for (int b = 0; b < kLoadBatch; ++b) {
+            const int j = j0 + lane + 32 * b;
+            if (j < nchunk && k_lo + (int64_t)j * 8 < p.H)
+              *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) =
+                  normalize8_f2<T>(hv[b], rs2, g2[b]);
+          }
         }
       }
     }
