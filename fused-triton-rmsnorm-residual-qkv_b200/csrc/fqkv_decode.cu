@@ -40,6 +40,7 @@ namespace {
 constexpr int kNormWarps = 8;                  // warps 2 .. 9: norm, then epilogue
 constexpr int kNormThreads = kNormWarps * 32;
 constexpr int kThreads = 64 + kNormThreads;
+static_assert(kThreads == kDecodeThreads, "fqkv_kernels.cuh states the decode kernel's block size");
 constexpr int kMaxCluster = 8;
 constexpr int kTileRows = 128;      // rows of W per MMA (UMMA M)
 constexpr int kKBlock = 64;         // K elements per stage (128 bytes of 16-bit data)

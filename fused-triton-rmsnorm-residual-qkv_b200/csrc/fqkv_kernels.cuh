@@ -291,6 +291,9 @@ cudaError_t launch_prepass(const PrepassParams& p, bool bf16, bool pdl, cudaStre
 cudaError_t launch_simt(const SimtParams& p, bool bf16, bool pdl, cudaStream_t stream);
 
 // Fused decode schedule chosen on the host.
+// Threads of the fused decode kernel: a TMA producer warp, an MMA warp, 8 norm/epilogue warps.
+constexpr int kDecodeThreads = 64 + 8 * 32;
+
 struct DecodeConfig {
   int mpad;     // token columns of the MMA (16, 32 or 64)
   int nt;       // 128-row W tiles per CTA (1 or 2)
@@ -325,6 +328,7 @@ struct GemmConfig {
   int stages;
   int grid;
   size_t smem;
+  int pair;     // 1: 2-CTA clusters computing 256-row tiles (tcgen05 cta_group::2)
 };
 int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg);
 cudaError_t launch_gemm(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,

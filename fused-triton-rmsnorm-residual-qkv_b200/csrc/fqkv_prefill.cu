@@ -15,6 +15,7 @@
 // the CTAs running at the same time share weight tiles in L2.
 // Every wait is bounded; a timeout sets the device status word and the CTA drains
 // its loads and MMAs, frees TMEM and returns.
+#include <cstdlib>
 #include <type_traits>
 
 #include "fqkv_kernels.cuh"
@@ -176,19 +177,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c0, v);
         tmem_wait_ld();
         const int n0 = nb * BN + c0;
+        const int cols = BN - c0 < 32 ? BN - c0 : 32;  // the last chunk of a tile may be narrower
         if (m < p.M) {
           uint32_t packed[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             packed[e] = (uint32_t)Elem<T>::from_f(__uint_as_float(v[2 * e])) |
                         ((uint32_t)Elem<T>::from_f(__uint_as_float(v[2 * e + 1])) << 16);
-          if (vec_ok && n0 + 32 <= p.N) {
+          if (vec_ok && cols == 32 && n0 + 32 <= p.N) {
             uint4* dst = reinterpret_cast<uint4*>(orow + n0);
 #pragma unroll
             for (int g = 0; g < 4; ++g)
               dst[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
           } else {
-            for (int e = 0; e < 32; ++e)
+            for (int e = 0; e < cols; ++e)
               if (n0 + e < p.N) orow[n0 + e] = (uint16_t)(packed[e >> 1] >> ((e & 1) * 16));
           }
         }
@@ -205,6 +207,212 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a 2-CTA cluster computes 256 x BN tiles.  CTA `rank`
+// loads rows [256 mb + 128 rank, +128) of A and rows [BN nb + (BN/2) rank, +BN/2) of B
+// into the same shared-memory offsets; the even CTA's MMA thread issues one
+// tcgen05.mma.cta_group::2 per 16-wide K slice, reading both CTAs' halves, and D's rows
+// [128 rank, +128) land in CTA `rank`'s TMEM.  Per SM that is half the B-operand traffic
+// of a 128 x BN tile for the same FLOPs.  Barriers:
+//   full[s]   (even CTA) both CTAs' loads of stage s, counted by TMA complete_tx;
+//   empty[s]  (each CTA) stage s consumed: one commit multicast to both CTAs;
+//   tfull[b]  (each CTA) accumulator b ready: one commit multicast to both CTAs;
+//   tempty[b] (even CTA) accumulator b drained: one arrive per epilogue warp of both CTAs;
+//   done      (each CTA) every MMA retired (multicast), before TMEM is freed.
+template <typename T, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p, const int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const GLayout L = make_glayout(stages, BN / 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done_bar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
+  constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256u : 512u;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles = p.tiles_m * p.tiles_n;  // tiles_m counts 256-row tiles
+  const int KB = p.kb_total;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(done_bar, 1);
+    fence_mbarrier_init_cluster();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs have initialised their barriers and allocated TMEM
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      pdl_wait();  // A is written by the pre-pass
+      const uint32_t half_bytes = L.stage_bytes;
+      bool ok = true;
+      int s = 0, round = 0, issued = 0;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1);
+          if (!ok) break;
+          // The even CTA's full[s] counts both CTAs' bytes.
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * half_bytes);
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+          uint8_t* st = smem + s * L.stage_bytes;
+          tma_load_2d_pair(st, &tmA, bar, kb * kKBlock, mb * 2 * kBM + (int)rank * kBM);
+          tma_load_2d_pair(st + kATileBytes, &tmB, bar, kb * kKBlock, nb * BN + (int)rank * (BN / 2));
+          ++issued;
+          if (++s == stages) {
+            s = 0;
+            ++round;
+          }
+        }
+      }
+      // Every load of the pair completes on the even CTA's full barriers: that CTA waits for
+      // the last `stages` of them (bounded), and both CTAs meet at the closing cluster
+      // barrier, so neither leaves with a load of the pair in flight.
+      if (rank == 0)
+        for (int j = max(0, issued - stages); j < issued; ++j) mbar_wait<true>(&full[j % stages], (j / stages) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0) {
+      if (rank == 0) {
+        const uint32_t idesc = make_idesc_f16(2 * kBM, BN, std::is_same<T, __nv_bfloat16>::value);
+        bool ok = true;
+        int s = 0, round = 0, li = 0;
+        for (int t = pair; t < tiles && ok; t += npairs, ++li) {
+          const int buf = li & 1, use = li >> 1;
+          if (use > 0) ok = mbar_wait<true>(&tempty[buf], (use - 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * BN;
+          for (int kb = 0; kb < KB; ++kb) {
+            ok = mbar_wait<true>(&full[s], round & 1);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(smem + s * L.stage_bytes);
+            const uint32_t b_base = a_base + kATileBytes;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_f16_pair(d_tmem, make_sw128_desc(a_base + kk * 32), make_sw128_desc(b_base + kk * 32), idesc,
+                            (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_commit_pair(&empty[s], 0x3);
+            if (++s == stages) {
+              s = 0;
+              ++round;
+            }
+          }
+          umma_commit_pair(&tfull[buf], 0x3);
+        }
+        umma_commit_pair(done_bar, 0x3);  // also on failure
+      }
+      mbar_wait<true>(done_bar, 0);  // every MMA retired before TMEM is freed
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    pdl_wait();  // out may still be read by the preceding grid
+    const int q = warp & 3;
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0) && ((p.ldo & 7) == 0);
+    const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    bool ok = true;
+    int li = 0;
+    for (int t = pair; t < tiles && ok; t += npairs, ++li) {
+      const int buf = li & 1, use = li >> 1;
+      ok = mbar_wait<true>(&tfull[buf], use & 1);
+      if (!ok) break;
+      tc_fence_after();
+      const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+      const int64_t m = (int64_t)mb * 2 * kBM + (int64_t)rank * kBM + q * 32 + lane;
+      uint16_t* orow = p.out + m * p.ldo;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c0, v);
+        tmem_wait_ld();
+        const int n0 = nb * BN + c0;
+        if (m < p.M) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) packed[e] = Elem<T>::from_f2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+          if (vec_ok && n0 + 32 <= p.N) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + n0);
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              dst[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (n0 + e < p.N) orow[n0 + e] = (uint16_t)(packed[e >> 1] >> ((e & 1) * 16));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty0 + buf * 8);
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // neither CTA frees TMEM or leaves while the pair may still use it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+template <typename T, int BN>
+cudaError_t launch_pair_bn(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
+                           bool pdl, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<T, BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  cfg.gridDim = dim3((unsigned)c.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = c.smem;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  int na = 1;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p, c.stages);
 }
 
 template <typename T, int BN>
@@ -233,6 +441,14 @@ cudaError_t launch_bn(const GemmConfig& c, const CUtensorMap& tmA, const CUtenso
 template <typename T>
 cudaError_t launch_t(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
                      bool pdl, cudaStream_t stream) {
+  if (c.pair) {
+    switch (c.bn) {
+      case 128: return launch_pair_bn<T, 128>(c, tmA, tmB, p, pdl, stream);
+      case 192: return launch_pair_bn<T, 192>(c, tmA, tmB, p, pdl, stream);
+      case 256: return launch_pair_bn<T, 256>(c, tmA, tmB, p, pdl, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (c.bn) {
     case 128: return launch_bn<T, 128>(c, tmA, tmB, p, pdl, stream);
     case 192: return launch_bn<T, 192>(c, tmA, tmB, p, pdl, stream);
@@ -245,29 +461,48 @@ cudaError_t launch_t(const GemmConfig& c, const CUtensorMap& tmA, const CUtensor
 
 constexpr size_t kGemmSmemLimit = 232448;
 
-// Tile width BN: the candidate with the fewest "tile-waves x BN" (time proxy with one
-// CTA per SM), ties going to the wider tile; ring depth as deep as shared memory allows.
+// Tile width BN: the candidate with the fewest "tile-waves x (BN + A share)" (time proxy
+// with one CTA per SM), ties going to the wider tile; ring depth as deep as shared memory
+// allows.  FQKV_GEMM_BN restricts the choice.
 int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg) {
   (void)H;
-  const int tiles_m = (M + kBM - 1) / kBM;
+  const int force_bn = [] {
+    const char* v = std::getenv("FQKV_GEMM_BN");
+    return (v && *v) ? std::atoi(v) : 0;
+  }();
+  // CTA pairs (256-row tiles) for M > 128 unless FQKV_GEMM_PAIR=0.
+  const bool pair = M > kBM && [] {
+    const char* v = std::getenv("FQKV_GEMM_PAIR");
+    return !(v && *v) || std::atoi(v) != 0;
+  }();
+  const int units = pair ? sm_count / 2 : sm_count;  // concurrent tile workers
+  const int bm = pair ? 2 * kBM : kBM;
+  const int tiles_m = (M + bm - 1) / bm;
   int best_bn = 0;
   long best_cost = 0;
   for (int bn : {256, 192, 128}) {
+    if (force_bn && bn != force_bn) continue;
     const long tiles = (long)tiles_m * ((N + bn - 1) / bn);
-    const long waves = (tiles + sm_count - 1) / sm_count;
-    const long cost = waves * bn;
+    const long waves = (tiles + units - 1) / units;
+    // A tile-wave costs its width plus a fixed share for the A operand, which every tile
+    // reloads whatever its width (measured on B200: at M = 2048 / 8192, BN = 256 beats the
+    // narrower tiles although they fill the last wave better).
+    const long cost = waves * (bn + 96);
     if (best_bn == 0 || cost < best_cost) {
       best_bn = bn;
       best_cost = cost;
     }
   }
+  if (best_bn == 0) return FQKV_ERR_SCHEDULE;
   GemmConfig c{};
   c.bn = best_bn;
+  c.pair = pair ? 1 : 0;
+  const int b_rows = pair ? c.bn / 2 : c.bn;  // B rows each CTA loads per stage
   c.stages = 2;
-  while (c.stages < 8 && 1024 + make_glayout(c.stages + 1, c.bn).total <= kGemmSmemLimit) ++c.stages;
-  c.smem = 1024 + make_glayout(c.stages, c.bn).total;
+  while (c.stages < 8 && 1024 + make_glayout(c.stages + 1, b_rows).total <= kGemmSmemLimit) ++c.stages;
+  c.smem = 1024 + make_glayout(c.stages, b_rows).total;
   const long tiles = (long)tiles_m * ((N + c.bn - 1) / c.bn);
-  c.grid = (int)(tiles < sm_count ? tiles : sm_count);
+  c.grid = (int)(tiles < units ? tiles : units) * (pair ? 2 : 1);
   *cfg = c;
   return 0;
 }

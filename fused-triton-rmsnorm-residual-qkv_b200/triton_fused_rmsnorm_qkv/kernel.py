@@ -12,12 +12,12 @@ Where the reference dispatches between two Triton kernels at M = 32 rows
 (kernel.py:360, :406) and picks tiles by autotuning (kernel.py:122-128, :264-268), the
 library chooses one of its kernel families from (M, H, N, SM count):
 
-* ``decode``  (M <= 32): one fused kernel -- swap-AB tcgen05 MMA, the weight streamed
+* ``decode``  (M <= 64): one fused kernel -- swap-AB tcgen05 MMA, the weight streamed
   by TMA, K split across a thread-block cluster whose CTAs exchange row sums of
   squares and partial tiles through distributed shared memory.
-* ``split``   (32 < M <= 128): norm pre-pass + the same swap-AB GEMM reading the
-  normalised rows by TMA.
-* ``prefill`` (M > 128): norm pre-pass + persistent 128 x BN tcgen05 GEMM.
+* ``split``   (M <= 64 when no decode configuration fits the device, or when forced; up
+  to M = 128): norm pre-pass + a stream-K swap-AB GEMM reading the normalised rows by TMA.
+* ``prefill`` (M > 64): norm pre-pass + persistent 128 x BN tcgen05 GEMM.
 * ``simt``    any shape/stride the TMA paths cannot take (H % 8 != 0, unaligned data).
 
 Extensions (keyword-only, so the reference call sites keep working): ``residual_out``

@@ -105,7 +105,8 @@ def _split_bytes(M, H, N):
 @pytest.mark.parametrize("M,H,sched,expect", [
     (1, 4096, _lib.SCHED_AUTO, 0),                  # fused decode: no scratch
     (16, 4096, _lib.SCHED_DECODE, 0),
-    (64, 4096, _lib.SCHED_AUTO, _split_bytes(64, 4096, 6144)),   # pre-pass + stream-K
+    (64, 4096, _lib.SCHED_AUTO, 0),                 # fused decode up to M = 64
+    (65, 4096, _lib.SCHED_AUTO, (65 * 4096 * 2 + 255) // 256 * 256),   # prefill: pre-pass scratch
     (16, 4096, _lib.SCHED_SPLIT, _split_bytes(16, 4096, 6144)),
     (2048, 4096, _lib.SCHED_PREFILL, 2048 * 4096 * 2),           # pre-pass scratch only
     (7, 4100, _lib.SCHED_AUTO, 0),                  # H % 8 != 0 -> SIMT, no scratch
