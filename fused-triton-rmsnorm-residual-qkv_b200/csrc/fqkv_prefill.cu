@@ -444,7 +444,6 @@ cudaError_t launch_t(const GemmConfig& c, const CUtensorMap& tmA, const CUtensor
   if (c.pair) {
     switch (c.bn) {
       case 128: return launch_pair_bn<T, 128>(c, tmA, tmB, p, pdl, stream);
-      case 192: return launch_pair_bn<T, 192>(c, tmA, tmB, p, pdl, stream);
       case 256: return launch_pair_bn<T, 256>(c, tmA, tmB, p, pdl, stream);
       default: return cudaErrorInvalidValue;
     }
@@ -482,6 +481,9 @@ int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg) {
   long best_cost = 0;
   for (int bn : {256, 192, 128}) {
     if (force_bn && bn != force_bn) continue;
+    // 256 x 192 pair tiles (96 B rows per CTA) measured 2-3x slower than 256 x 256 on
+    // B200, and their results are not covered by the tests: pairs use 256 or 128.
+    if (pair && bn == 192) continue;
     const long tiles = (long)tiles_m * ((N + bn - 1) / bn);
     const long waves = (tiles + units - 1) / units;
     // A tile-wave costs its width plus a fixed share for the A operand, which every tile
