@@ -470,7 +470,7 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
         "ms_per_step": round(ms_max / args.steps, 6),
         "us_per_step": round(ms_max / args.steps * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "strong",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) x/residual, 1+0.1N(0,1) gain, N(0,0.02) weights), random-init",

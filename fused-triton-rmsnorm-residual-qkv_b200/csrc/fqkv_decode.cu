@@ -19,9 +19,10 @@
 //              exchange per-row partial sums of squares across the cluster through
 //              DSMEM, then normalise in place: dtype((h * rstd) * g) (baseline.py:59-62).
 //              The normalised activations never leave shared memory.
-//              Epilogue: TMEM -> registers -> shared memory; each CTA reduces 1/C of
-//              the tile over the cluster's C partial tiles (16-byte DSMEM loads, fixed
-//              rank order: deterministic) and stores it.
+//              Epilogue: TMEM -> registers -> shared memory; each CTA bulk-copies
+//              the slice of its partial tile that rank o owns into rank o's idle ring
+//              (cp.async.bulk shared::cta -> shared::cluster), and each owner sums the C
+//              partials of its slice in rank order (deterministic) and stores it.
 // The host sizes (NT, C, STAGES) so that all clusters are resident at once
 // (cudaOccupancyMaxActiveClusters): a second wave would double the time.
 // Every wait is bounded (fqkv_device.cuh); after a timeout the kernel drains its own
@@ -61,8 +62,8 @@ __host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int 
   L.red = L.gain + (uint32_t)nkb_max * kKBlock * 4;    // [kMaxCluster][mpad] floats
   L.rowp = L.red + kMaxCluster * mpad * 4;            // [mpad] floats
   L.rstd = L.rowp + mpad * 4;                         // [mpad] floats
-  L.bars = (L.rstd + mpad * 4 + 7) & ~7u;             // full[S], empty[S], accum, normed, sum, part, acts
-  L.tmem_slot = L.bars + (2 * stages + 5) * 8;
+  L.bars = (L.rstd + mpad * 4 + 7) & ~7u;   // full[S], empty[S], accum, normed, sum, part, acts, recv
+  L.tmem_slot = L.bars + (2 * stages + 6) * 8;
   L.total = L.tmem_slot + 16;
   return L;
 }
@@ -89,9 +90,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* sum_bar = accum_bar + 2;
   uint64_t* part_bar = accum_bar + 3;  // every CTA of the cluster has written its partial tile
   uint64_t* acts_bar = accum_bar + 4;  // the norm warps have issued their activation loads
+  uint64_t* recv_bar = accum_bar + 5;  // the peers' slices of this CTA's share have landed
   float* gain_s = reinterpret_cast<float*>(smem + L.gain);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
-  float* part = reinterpret_cast<float*>(ring);  // [NT][MPAD][128] partial tile, aliases the ring
+  // The epilogue reuses the ring once the MMAs have retired: this CTA's partial tile
+  // [MPAD][NT][128] floats, then C receive slots of kSlotBytes for the peers' slices of the
+  // part of the tile this CTA reduces.
+  float* part = reinterpret_cast<float*>(ring);
+  constexpr uint32_t kPartBytes = NT * MPAD * kTileRows * 4;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t C = gridDim.x;
@@ -113,6 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(sum_bar, 1);      // local arrive + C * MPAD * 4 bytes of st.async from the cluster
     mbar_init(part_bar, C);     // one (relaxed, fenced) arrive per CTA of the cluster
     mbar_init(acts_bar, 1);
+    mbar_init(recv_bar, 1);     // local arrive + the peers' bulk copies (complete_tx)
     fence_mbarrier_init_cluster();
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tmW);
@@ -206,8 +213,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j < nchunk && k < p.H) load_gain8_raw(p.g, p.gdt, k, graw[i]);
       }
     };
-    // This CTA expects C * MPAD row sums (4 bytes each) from the cluster's st.async writes.
-    if (et == 0) mbar_arrive_expect_tx_cluster(sum_bar, C * MPAD * 4);
+    // The tile's partial sums are reduced in 16-byte quads (4 output features): quad
+    // f = ((m * NT + nt) * 128 + row) / 4 for token m < M; rank o reduces [F(o), F(o+1)).
+    const uint32_t total4 = (uint32_t)(NT * p.M * (kTileRows / 4));
+    auto share = [&](uint32_t o) { return (o * total4) / C; };
+    const uint32_t slot_bytes = 16u * ((NT * MPAD * (kTileRows / 4) + C - 1) / C);
+    // This CTA expects C * MPAD row sums (4 bytes each) from the cluster's st.async writes,
+    // and later C - 1 bulk copies of its share of the tile.
+    if (et == 0) {
+      mbar_arrive_expect_tx_cluster(sum_bar, C * MPAD * 4);
+      mbar_arrive_expect_tx_cluster(recv_bar, (C - 1) * 16u * (share(rank + 1) - share(rank)));
+    }
     if (static_w) issue_gain();
     pdl_wait();
     if (!static_w) issue_gain();
@@ -360,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("bar.sync 1, 256;" ::: "memory");
     if (et == 0) mbar_arrive(normed_bar);
 
-    // Epilogue: TMEM -> registers -> this CTA's partial tile in shared memory.
+    // Epilogue: TMEM -> registers -> this CTA's partial tile in shared memory, laid out
+    // [m][nt][row] so that every rank's share is one contiguous byte range.
     ok = mbar_wait(accum_bar, 0) && ok;
     tc_fence_after();
     const int q = warp & 3;             // TMEM lane quadrant this warp may access
@@ -375,43 +392,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + nt * MPAD + c0, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) part[(nt * MPAD + c0 + e) * kTileRows + row] = __uint_as_float(v[e]);
+        for (int e = 0; e < 16; ++e) part[((c0 + e) * NT + nt) * kTileRows + row] = __uint_as_float(v[e]);
       }
     }
     tc_fence_before();
+    // The bulk copies read the partial tile through the async proxy.
+    fence_proxy_async_smem();
     // One release per CTA: the CTA barrier orders every thread's partial-tile writes before
-    // thread 0's cluster fence, which the relaxed remote arrives then publish.
+    // thread 0's cluster fence, which the relaxed remote arrives then publish.  An arrival
+    // also says that this CTA's MMAs have retired, so its ring may receive the peers' slices.
     asm volatile("bar.sync 1, 256;" ::: "memory");
     if (et == 0) {
       fence_acq_rel_cluster();
       for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
     }
     ok = mbar_wait<true>(part_bar, 0) && ok;
-    // Reduce 1/C of the tile across the cluster and store it.  A step covers 4 consecutive
-    // output features: one 16-byte DSMEM load per rank, all C issued before the sum, which
-    // runs in rank order (deterministic).
-    const int64_t total4 = (int64_t)NT * p.M * (kTileRows / 4);
-    const int64_t f0 = (rank * total4) / C, f1 = ((rank + 1) * total4) / C;
-    const uint32_t part_base = smem_u32(part);
+    // Lane c of warp 2 sends rank c's share of this CTA's partial tile to slot `rank` of
+    // rank c's ring.
+    if (warp == 2 && (uint32_t)lane < C && (uint32_t)lane != rank) {
+      const uint32_t o = (uint32_t)lane, f0 = share(o), nb = 16u * (share(o + 1) - f0);
+      if (nb > 0)
+        bulk_copy_to_peer(mapa_shared(smem_u32(ring) + kPartBytes + rank * slot_bytes, o), smem_u32(part) + 16u * f0,
+                          nb, mapa_shared(smem_u32(recv_bar), o));
+    }
+    ok = mbar_wait<true>(recv_bar, 0) && ok;
+    // Every copy into this CTA has landed, so their sources have been read: this thread
+    // makes no further access to a peer's shared memory, nor a peer to this CTA's.
+    cluster_arrive_release_thread();
+    // Reduce this CTA's share: the C partials of each quad in rank order (deterministic).
+    const uint32_t f0 = share(rank), f1 = share(rank + 1);
+    const float4* part4 = reinterpret_cast<const float4*>(part);
+    const float4* recv4 = reinterpret_cast<const float4*>(ring + kPartBytes);
     const bool vec_store = (p.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 7) == 0;
-    for (int64_t f = f0 + et; f < f1; f += kNormThreads) {
-      const int nl = (int)(f % (kTileRows / 4)) * 4;
-      const int64_t rest = f / (kTileRows / 4);
-      const int nt = (int)(rest % NT);
-      const int m = (int)(rest / NT);
-      const uint32_t off = (uint32_t)(((nt * MPAD + m) * kTileRows + nl) * 4);
-      float4 v[kMaxCluster];
-#pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c)
-        v[c] = (uint32_t)c < C ? ld_cluster_f32x4(mapa_shared(part_base + off, c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t f = f0 + et; f < f1; f += kNormThreads) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c) {
-        acc.x += v[c].x;
-        acc.y += v[c].y;
-        acc.z += v[c].z;
-        acc.w += v[c].w;
+      for (uint32_t c = 0; c < C; ++c) {
+        const float4 v = c == rank ? part4[f] : recv4[c * (slot_bytes / 16) + (f - f0)];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
       }
+      const int nl = (int)(f % (kTileRows / 4)) * 4;
+      const uint32_t mn = f / (kTileRows / 4);
+      const int nt = (int)(mn % NT), m = (int)(mn / NT);
       const int n = n_base + nt * kTileRows + nl;
       uint16_t* dst = p.out + (int64_t)m * p.ldo + n;
       if (vec_store && n + 3 < p.N) {
@@ -423,8 +447,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (n + e < p.N) dst[e] = Elem<T>::from_f(a4[e]);
       }
     }
-    // This thread's last access to a peer's shared memory.
-    cluster_arrive_release_thread();
     (void)ok;
   }
 
@@ -537,8 +559,9 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
       if ((KB + cl - 1) / cl * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
-      // The epilogue's partial tile aliases the ring.
-      const int min_stages = (nt * mpad * kTileRows * 4 + nt * kWTileBytes - 1) / (nt * kWTileBytes);
+      // The epilogue's partial tile and its C receive slots alias the ring.
+      const int epi_bytes = nt * mpad * kTileRows * 4 + cl * 16 * ((nt * mpad * (kTileRows / 4) + cl - 1) / cl);
+      const int min_stages = (epi_bytes + nt * kWTileBytes - 1) / (nt * kWTileBytes);
       for (int st = 16; st >= max(2, min_stages); --st) {
         if (force_s && st != force_s) continue;
         DecodeConfig t{mpad, nt, st, cl, 0};
