@@ -93,11 +93,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* recv_bar = accum_bar + 5;  // the peers' slices of this CTA's share have landed
   float* gain_s = reinterpret_cast<float*>(smem + L.gain);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
-  // The epilogue reuses the ring once the MMAs have retired: this CTA's partial tile
-  // [MPAD][NT][128] floats, then C receive slots of kSlotBytes for the peers' slices of the
-  // part of the tile this CTA reduces.
+  // The epilogue reuses buffers the MMAs no longer need: this CTA's partial tile
+  // [MPAD][NT][128] floats at the start of the ring, and C receive slots for the peers'
+  // slices of the part of the tile this CTA reduces, in the normalised-activation buffer
+  // when they fit there (else after the partial tile in the ring).
   float* part = reinterpret_cast<float*>(ring);
   constexpr uint32_t kPartBytes = NT * MPAD * kTileRows * 4;
+  uint8_t* recv = p.recv_in_normed ? normed : ring + kPartBytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t C = gridDim.x;
@@ -412,8 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 2 && (uint32_t)lane < C && (uint32_t)lane != rank) {
       const uint32_t o = (uint32_t)lane, f0 = share(o), nb = 16u * (share(o + 1) - f0);
       if (nb > 0)
-        bulk_copy_to_peer(mapa_shared(smem_u32(ring) + kPartBytes + rank * slot_bytes, o), smem_u32(part) + 16u * f0,
-                          nb, mapa_shared(smem_u32(recv_bar), o));
+        bulk_copy_to_peer(mapa_shared(smem_u32(recv) + rank * slot_bytes, o), smem_u32(part) + 16u * f0, nb,
+                          mapa_shared(smem_u32(recv_bar), o));
     }
     ok = mbar_wait<true>(recv_bar, 0) && ok;
     // Every copy into this CTA has landed, so their sources have been read: this thread
@@ -422,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Reduce this CTA's share: the C partials of each quad in rank order (deterministic).
     const uint32_t f0 = share(rank), f1 = share(rank + 1);
     const float4* part4 = reinterpret_cast<const float4*>(part);
-    const float4* recv4 = reinterpret_cast<const float4*>(ring + kPartBytes);
+    const float4* recv4 = reinterpret_cast<const float4*>(recv);
     const bool vec_store = (p.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 7) == 0;
     for (uint32_t f = f0 + et; f < f1; f += kNormThreads) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -559,12 +561,16 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
       if ((KB + cl - 1) / cl * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
-      // The epilogue's partial tile and its C receive slots alias the ring.
-      const int epi_bytes = nt * mpad * kTileRows * 4 + cl * 16 * ((nt * mpad * (kTileRows / 4) + cl - 1) / cl);
+      // The epilogue's partial tile aliases the ring; its C receive slots go into the
+      // normalised-activation buffer when they fit there, else after the partial tile.
+      const int part_bytes = nt * mpad * kTileRows * 4;
+      const int recv_bytes = cl * 16 * ((nt * mpad * (kTileRows / 4) + cl - 1) / cl);
+      const int recv_in_normed = recv_bytes <= (KB + cl - 1) / cl * mpad * 128 ? 1 : 0;
+      const int epi_bytes = part_bytes + (recv_in_normed ? 0 : recv_bytes);
       const int min_stages = (epi_bytes + nt * kWTileBytes - 1) / (nt * kWTileBytes);
       for (int st = 16; st >= max(2, min_stages); --st) {
         if (force_s && st != force_s) continue;
-        DecodeConfig t{mpad, nt, st, cl, 0};
+        DecodeConfig t{mpad, nt, st, cl, 0, recv_in_normed};
         t.smem = decode_smem_bytes(t, KB);
         if (t.smem > kSmemLimit) continue;
         const int resident = max_active_clusters(t, tiles);
@@ -602,6 +608,7 @@ cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const D
   cfg.numAttrs = na;
   DecodeParams q = p;
   q.pre_stages = env_int("FQKV_DECODE_PRE", 2);
+  q.recv_in_normed = c.recv_in_normed;
   return cudaLaunchKernelEx(&cfg, k, tmW, q, c.stages);
 }
 

@@ -50,6 +50,8 @@ struct DecodeParams {
   int nkb_max;        // max k-blocks of one CTA's K slice
   int flags;
   int pre_stages;     // weight stages issued before the activation loads are out
+  int recv_in_normed; // the epilogue's receive slots use the (then idle) normalised-activation
+                      // buffer instead of the ring
 };
 
 struct StreamKParams {
@@ -300,6 +302,7 @@ struct DecodeConfig {
   int stages;   // ring depth
   int cluster;  // CTAs splitting K (cluster size)
   size_t smem;  // dynamic shared memory bytes
+  int recv_in_normed;  // see DecodeParams
 };
 
 int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg);
