@@ -18,7 +18,11 @@ residual add with the updated residual returned).  32 distinct seeded weight set
   roofline   achieved GB/s of the dominant kernel vs the measured HBM copy peak;
   cpu_baseline  the CPU oracle (a restatement of the reference's baseline.py) on a
              bounded sample of the same workload, rank 0 only at N=1;
-  detail     M=1/4/64 decode and M=2048 prefill (TFLOPS) measured the same way.
+  detail     the other configs measured the same way: Llama-3-8B decode M=1/4/16/64
+             (bf16, fp16), Qwen2-7B decode M=1/16/64 (with and without residual),
+             Llama-3-70B M=1/16/256, the post-attention gate/up shape (N=28672), prefill
+             M=512/2048/8192 (TFLOPS), the unfused PyTorch path (cuBLAS) on the same
+             inputs as the GPU comparator, and a streaming-read bandwidth for context.
 With N > 1 (torchrun) the layer is head-sharded column-parallel: each rank owns N/P
 weight rows and computes them with replicated inputs; no collective runs inside the
 timed region.  After timing, an NCCL all-gather reassembles one step for a check
@@ -55,6 +59,9 @@ WORKLOADS = {
     "qwen2-7b-decode": dict(H=3584, n_q=28, n_kv=4, d=128, M=16, eps=1e-6, res=True, sets=32),
     "llama3-8b-prefill": dict(H=4096, n_q=32, n_kv=8, d=128, M=2048, eps=1e-5, res=True, sets=4),
     "llama3-70b": dict(H=8192, n_q=64, n_kv=8, d=128, M=1, eps=1e-5, res=True, sets=16),
+    # post-attention residual add + RMSNorm + packed [W_gate; W_up] (N = 2 x 14336), as
+    # 224 "heads" of 128 rows so the same set builder applies (single GPU only)
+    "llama3-8b-mlp": dict(H=4096, n_q=224, n_kv=0, d=128, M=16, eps=1e-5, res=True, sets=8),
 }
 
 
@@ -303,6 +310,91 @@ def run_reference(args, wl: dict, M: int) -> dict:
 METRIC = "fused-op µs & HBM GB/s (% of 8 TB/s) at M=1/16, Llama-3-8B shape; prefill TFLOPS"
 
 
+# ----------------------------------------------------------------------------- detail
+# (label, workload, M, dtype name, has residual, weight sets, comparator).  The MLP entry
+# is the same op on the post-attention side of a Llama-3-8B layer: residual add +
+# post_attention_layernorm + the packed [W_gate; W_up] projection (N = 2 x 14336).
+DETAIL = [
+    ("llama3-8b_decode_M1", "llama3-8b-decode", 1, "bf16", True, 32, True),
+    ("llama3-8b_decode_M4", "llama3-8b-decode", 4, "bf16", True, 32, False),
+    ("llama3-8b_decode_M16", "llama3-8b-decode", 16, "bf16", True, 32, True),
+    ("llama3-8b_decode_M64", "llama3-8b-decode", 64, "bf16", True, 32, False),
+    ("llama3-8b_decode_M1_fp16", "llama3-8b-decode", 1, "fp16", True, 32, False),
+    ("llama3-8b_decode_M16_fp16", "llama3-8b-decode", 16, "fp16", True, 32, False),
+    ("qwen2-7b_decode_M1", "qwen2-7b-decode", 1, "bf16", True, 32, False),
+    ("qwen2-7b_decode_M16", "qwen2-7b-decode", 16, "bf16", True, 32, False),
+    ("qwen2-7b_decode_M64", "qwen2-7b-decode", 64, "bf16", True, 32, False),
+    ("qwen2-7b_decode_M16_no_residual", "qwen2-7b-decode", 16, "bf16", False, 32, False),
+    ("llama3-70b_M1", "llama3-70b", 1, "bf16", True, 16, False),
+    ("llama3-70b_M16", "llama3-70b", 16, "bf16", True, 16, False),
+    ("llama3-70b_M256", "llama3-70b", 256, "bf16", True, 8, False),
+    ("llama3-8b_mlp_gate_up_M1", "llama3-8b-mlp", 1, "bf16", True, 8, False),
+    ("llama3-8b_mlp_gate_up_M16", "llama3-8b-mlp", 16, "bf16", True, 8, False),
+    ("llama3-8b_prefill_M512", "llama3-8b-prefill", 512, "bf16", True, 4, False),
+    ("llama3-8b_prefill_M2048", "llama3-8b-prefill", 2048, "bf16", True, 4, True),
+    ("llama3-8b_prefill_M8192", "llama3-8b-prefill", 8192, "bf16", True, 4, False),
+]
+
+
+def torch_step_fn(sets, eps):
+    """The unfused PyTorch path (the reference's baseline.py semantics) on the GPU."""
+    from triton_fused_rmsnorm_qkv import rmsnorm_residual_qkv
+
+    S = len(sets)
+
+    def step(i):
+        x, r, g, w = sets[i % S]
+        rmsnorm_residual_qkv(x, r, g, w, eps)
+
+    return step
+
+
+def hbm_read_peak_gbs(dev) -> float:
+    """Streaming read bandwidth of a 4 GiB bf16 tensor (torch.sum), for context beside the
+    measured copy peak: a decode op is almost entirely a read."""
+    t = torch.ones(2 << 30, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        t.sum()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(10):
+        t.sum()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    gbs = t.numel() * 2 * 10 / (e0.elapsed_time(e1) / 1e3) / 1e9
+    del t
+    return gbs
+
+
+def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
+    from triton_fused_rmsnorm_qkv import _lib
+
+    dtypes = {"bf16": (torch.bfloat16, _lib.BF16), "fp16": (torch.float16, _lib.F16)}
+    detail = {"hbm_read_peak_gbs_torch_sum": round(hbm_read_peak_gbs(dev), 1)}
+    for label, wname, mm, dname, res, n_sets, comparator in DETAIL:
+        wl = dict(WORKLOADS[wname], res=res, sets=n_sets)
+        dt, dcode = dtypes[dname]
+        ss, layout = make_sets(wl, mm, dt, dev, 1, 0, n_sets)
+        H, N = wl["H"], layout.n_out
+        k = 2000 if mm <= 64 else (200 if mm <= 512 else (40 if mm <= 2048 else 12))
+        t_ms = time_graph(op_step_fn(ss, wl["eps"], mm), k, 5, dev) / k
+        b = algorithmic_bytes(mm, H, N, res)
+        fl = 2.0 * mm * N * H
+        entry = {"M": mm, "H": H, "N": N, "dtype": dname, "residual": res, "us": round(t_ms * 1e3, 3),
+                 "GB/s": round(b / t_ms / 1e6, 1), "pct_of_measured_hbm": round(100 * b / t_ms / 1e6 / peaks["hbm_gbs"], 2),
+                 "TFLOPS": round(fl / t_ms / 1e9, 1),
+                 "pct_of_measured_bf16": round(100 * fl / t_ms / 1e9 / peaks["bf16_tflops"], 2),
+                 "schedule": _lib.SCHEDULE_NAMES[_lib.query_schedule(mm, H, N, dcode)["schedule"]]}
+        if comparator:
+            t_ref = time_graph(torch_step_fn(ss, wl["eps"]), k, 5, dev) / k
+            entry["torch_unfused_us"] = round(t_ref * 1e3, 3)
+            entry["speedup_vs_torch_unfused"] = round(t_ref / t_ms, 2)
+        detail[label] = entry
+        del ss
+    return detail
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def run_ours(args, wl: dict, M: int) -> dict | None:
     world, rank, local = dist_env()
@@ -352,9 +444,16 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
         from triton_fused_rmsnorm_qkv import fused_rmsnorm_residual_matmul
         from triton_fused_rmsnorm_qkv.sharding import gather_qkv
 
+        from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul as _fused_add
+
         x, r, g, w_loc = sets[0]
-        out_loc = fused_rmsnorm_residual_matmul(x, r, g, w_loc, wl["eps"])
+        out_loc, hid_loc = _fused_add(x, r, g, w_loc, wl["eps"])
         full = gather_qkv(out_loc, layout)
+        # Every rank computes the same updated residual from replicated inputs: gather them
+        # and require bit equality.
+        hids = [torch.empty_like(hid_loc) for _ in range(world)]
+        pg.all_gather(hids, hid_loc.contiguous())
+        hid_same = all(torch.equal(h.view(torch.int16), hids[0].view(torch.int16)) for h in hids)
         if rank == 0:
             gen = torch.Generator(device=dev).manual_seed(1000)
             torch.randn(1, M, H, generator=gen, device=dev)
@@ -366,6 +465,7 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
             d = (full.float() - ref.float())
             shard_check = {"max_abs_vs_unsharded": float(d.abs().max()),
                            "rel_l2_vs_unsharded": float(d.norm() / ref.float().norm()),
+                           "residual_bit_identical_across_ranks": bool(hid_same),
                            "gathered_with": "nccl all_gather"}
         barrier()
 
@@ -414,31 +514,11 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
            "path": "fused_add_rmsnorm_matmul (public API) with pinned host x/residual in, out/hidden back, "
                    "synchronised every step", "n_gpus_used": 1}
 
-    # ---- detail: the metric's other points, timed the same way (N=1 only)
+    # ---- detail: the metric's other points and the other configs, timed the same way,
+    # with the unfused PyTorch path (cuBLAS) as the GPU comparator (N=1 only)
     detail = {}
     if world == 1 and not args.no_detail:
-        for mm in (1, 4, 16, 64):
-            ss, _ = make_sets(wl, mm, dtype, dev, 1, 0, wl["sets"])
-            k = 2000
-            t_ms = time_graph(op_step_fn(ss, wl["eps"], mm), k, 5, dev) / k
-            b = algorithmic_bytes(mm, H, N_glob, wl["res"])
-            detail[f"decode_M{mm}"] = {"us": round(t_ms * 1e3, 3), "GB/s": round(b / t_ms / 1e6, 1),
-                                       "pct_of_8TBs": round(100 * b / t_ms / 1e6 / HBM_SPEC_GBS, 2),
-                                       "pct_of_measured_hbm": round(100 * b / t_ms / 1e6 / peaks["hbm_gbs"], 2),
-                                       "schedule": _lib.SCHEDULE_NAMES[_lib.query_schedule(mm, H, N_glob,
-                                                                                           _lib.BF16)["schedule"]]}
-            del ss
-        pf = WORKLOADS["llama3-8b-prefill"]
-        for mm in (512, 2048, 8192):
-            ss, _ = make_sets(pf, mm, dtype, dev, 1, 0, pf["sets"])
-            k = 40 if mm <= 2048 else 12
-            t_ms = time_graph(op_step_fn(ss, pf["eps"], mm), k, 3, dev) / k
-            fl = 2.0 * mm * N_glob * H
-            detail[f"prefill_M{mm}"] = {"us": round(t_ms * 1e3, 2), "TFLOPS": round(fl / t_ms / 1e9, 1),
-                                        "pct_of_2.25PF": round(100 * fl / t_ms / 1e9 / BF16_SPEC_TFLOPS, 2),
-                                        "pct_of_measured_bf16": round(
-                                            100 * fl / t_ms / 1e9 / peaks["bf16_tflops"], 2)}
-            del ss
+        detail = run_detail(wl, dev, peaks)
         torch.cuda.empty_cache()
 
     # ---- CPU baseline (rank 0, N=1): the oracle on a bounded sample

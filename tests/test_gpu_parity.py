@@ -84,6 +84,13 @@ def test_llama3_70b(M):
     run_case(M, *LLAMA70B, torch.bfloat16, seed=400 + M, sample_rows=64)
 
 
+@pytest.mark.parametrize("M", [1, 16])
+def test_post_attention_gate_up_shape(M):
+    """The same op on the post-attention side of a Llama-3-8B layer: residual add +
+    post_attention_layernorm + the packed [W_gate; W_up] projection (N = 2 x 14336)."""
+    run_case(M, 4096, 2 * 14336, torch.bfloat16, seed=500 + M)
+
+
 def test_cpu_ref_shape_on_gpu():
     """configs[0]'s shape (4 tokens, H=256, N=512) in bf16 (the kernels take 16-bit data)."""
     run_case(4, 256, 512, torch.bfloat16, seed=1)
