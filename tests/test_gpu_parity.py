@@ -84,6 +84,15 @@ def test_llama3_70b(M):
     run_case(M, *LLAMA70B, torch.bfloat16, seed=400 + M, sample_rows=64)
 
 
+@pytest.mark.parametrize("H,n_loc", [(4096, 3072), (4096, 1536), (4096, 768), (8192, 5120), (8192, 2560),
+                                      (8192, 1280)])
+@pytest.mark.parametrize("M", [1, 16])
+def test_head_sharded_local_shapes(M, H, n_loc):
+    """The per-rank problem of the head-sharded layout at 2, 4 and 8 GPUs (Llama-3-8B and
+    Llama-3-70B): N_OUT / P weight rows, replicated activations."""
+    run_case(M, H, n_loc, torch.bfloat16, seed=600 + M + n_loc)
+
+
 @pytest.mark.parametrize("M", [1, 16])
 def test_post_attention_gate_up_shape(M):
     """The same op on the post-attention side of a Llama-3-8B layer: residual add +
