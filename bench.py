@@ -406,6 +406,10 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
 
         import torch.distributed as dist
 
+        # Rank 0 prints exactly one JSON line on stdout: NCCL's own messages (e.g. its
+        # version banner) go to stderr unless the caller chose a destination.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = dist
 
