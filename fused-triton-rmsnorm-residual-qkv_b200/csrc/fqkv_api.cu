@@ -9,8 +9,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 
 #include "fqkv_kernels.cuh"
 
@@ -89,8 +91,25 @@ int get_encode(EncodeTiledFn* fn) {
 
 // 2-D K-major tensor map over a [rows, cols] matrix of 16-bit elements with row
 // stride ld (elements), 128-byte swizzle, box {64, box_rows}.
+// Encoded maps are cached by (address, shape, stride, box, dtype): a model calls the op
+// with the same weight (and often the same activation buffers) every step, and a map
+// holds only the address and the layout.
+using MapKey = std::tuple<const void*, int64_t, int64_t, int64_t, int, bool>;
+std::mutex g_map_mu;
+std::map<MapKey, CUtensorMap> g_map_cache;
+constexpr size_t kMapCacheMax = 1024;
+
 int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
              bool bf16) {
+  const MapKey key{base, rows, cols, ld, box_rows, bf16};
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) {
+      *map = it->second;
+      return 0;
+    }
+  }
   EncodeTiledFn enc;
   if (int rc = get_encode(&enc)) return rc;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -104,6 +123,9 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
   if (r != CUDA_SUCCESS)
     return fail(FQKV_ERR_ALIGN, "cuTensorMapEncodeTiled failed (%d) for a [%lld, %lld] matrix, ld %lld", (int)r,
                 (long long)rows, (long long)cols, (long long)ld);
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  if (g_map_cache.size() >= kMapCacheMax) g_map_cache.clear();
+  g_map_cache.emplace(key, *map);
   return 0;
 }
 
@@ -228,6 +250,29 @@ int validate(const Problem& p) {
 }
 
 }  // namespace
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device) and size:
+// the attribute only has to cover the largest request seen.
+cudaError_t ensure_smem_attr(const void* func, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_pair(func, dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& v = done[key];
+  if (bytes > v) v = bytes;
+  return cudaSuccess;
+}
+
 }  // namespace fqkv
 
 using namespace fqkv;

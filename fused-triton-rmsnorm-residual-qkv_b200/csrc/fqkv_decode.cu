@@ -516,7 +516,7 @@ int max_active_clusters(const DecodeConfig& c, int tiles) {
   }
   KernelFn k = pick_kernel(c.mpad, c.nt, true);
   int n = 0;
-  if (k && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem) == cudaSuccess) {
+  if (k && ensure_smem_attr(reinterpret_cast<const void*>(k), c.smem) == cudaSuccess) {
     cudaLaunchAttribute attr[2];
     int na = 0;
     cudaLaunchConfig_t cfg = base_config(c, tiles, attr, &na);
@@ -547,13 +547,29 @@ size_t decode_smem_bytes(const DecodeConfig& c, int kb_total) {
 // go to the deeper ring, then to the smaller cluster).
 // FQKV_DECODE_NT / FQKV_DECODE_CLUSTER / FQKV_DECODE_STAGES restrict the search.
 int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
-  DecodeConfig best{};
   const int mpad = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
   if (mpad == 0) return FQKV_ERR_SCHEDULE;
+  // Tuning overrides, read once per process.
+  static const int force_nt = env_int("FQKV_DECODE_NT", 0);
+  static const int force_c = env_int("FQKV_DECODE_CLUSTER", 0);
+  static const int force_s = env_int("FQKV_DECODE_STAGES", 0);
+  // The search below queries occupancy for many candidates; its result is cached per
+  // (device, MPAD, H, N, SM count, overrides), so a model's per-step calls skip it.
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int, int, int>, std::pair<int, DecodeConfig>> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, mpad, H, N, sm_count, force_nt, force_c, force_s);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      if (it->second.first == 0) *cfg = it->second.second;
+      return it->second.first;
+    }
+  }
+  DecodeConfig best{};
   const int KB = (H + kKBlock - 1) / kKBlock;
-  const int force_nt = env_int("FQKV_DECODE_NT", 0);
-  const int force_c = env_int("FQKV_DECODE_CLUSTER", 0);
-  const int force_s = env_int("FQKV_DECODE_STAGES", 0);
   long best_score = -1;
   for (int nt = 1; nt <= 2; ++nt) {
     if (force_nt && nt != force_nt) continue;
@@ -584,16 +600,20 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
       }
     }
   }
-  if (best_score < 0) return FQKV_ERR_SCHEDULE;
-  *cfg = best;
-  return 0;
+  const int rc = best_score < 0 ? FQKV_ERR_SCHEDULE : 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = std::make_pair(rc, best);
+  }
+  if (rc == 0) *cfg = best;
+  return rc;
 }
 
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream) {
   KernelFn k = pick_kernel(c.mpad, c.nt, bf16);
   if (!k) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(k), c.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[2];
   int na = 0;
@@ -607,7 +627,8 @@ cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const D
   }
   cfg.numAttrs = na;
   DecodeParams q = p;
-  q.pre_stages = env_int("FQKV_DECODE_PRE", 2);
+  static const int pre_stages = env_int("FQKV_DECODE_PRE", 2);  // read once per process
+  q.pre_stages = pre_stages;
   q.recv_in_normed = c.recv_in_normed;
   return cudaLaunchKernelEx(&cfg, k, tmW, q, c.stages);
 }

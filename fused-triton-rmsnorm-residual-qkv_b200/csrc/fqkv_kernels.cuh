@@ -289,6 +289,9 @@ __device__ __forceinline__ uint4 normalize8g(uint4 h, float rstd, const float4 (
 }
 
 // ------------------------------------------------------------------ launchers
+// Raise a kernel's dynamic shared-memory limit to `bytes` (cached per kernel and device).
+cudaError_t ensure_smem_attr(const void* func, size_t bytes);
+
 cudaError_t launch_prepass(const PrepassParams& p, bool bf16, bool pdl, cudaStream_t stream);
 cudaError_t launch_simt(const SimtParams& p, bool bf16, bool pdl, cudaStream_t stream);
 

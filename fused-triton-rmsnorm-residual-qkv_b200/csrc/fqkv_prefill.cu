@@ -392,7 +392,7 @@ template <typename T, int BN>
 cudaError_t launch_pair_bn(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
                            bool pdl, cudaStream_t stream) {
   auto kern = gemm_pair_kernel<T, BN>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), c.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -419,7 +419,7 @@ template <typename T, int BN>
 cudaError_t launch_bn(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
                       bool pdl, cudaStream_t stream) {
   auto kern = gemm_kernel<T, BN>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), c.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -465,15 +465,16 @@ constexpr size_t kGemmSmemLimit = 232448;
 // allows.  FQKV_GEMM_BN restricts the choice.
 int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg) {
   (void)H;
-  const int force_bn = [] {
+  static const int force_bn = [] {  // tuning overrides, read once per process
     const char* v = std::getenv("FQKV_GEMM_BN");
     return (v && *v) ? std::atoi(v) : 0;
   }();
   // CTA pairs (256-row tiles) for M > 128 unless FQKV_GEMM_PAIR=0.
-  const bool pair = M > kBM && [] {
+  static const bool pair_allowed = [] {
     const char* v = std::getenv("FQKV_GEMM_PAIR");
     return !(v && *v) || std::atoi(v) != 0;
   }();
+  const bool pair = M > kBM && pair_allowed;
   const int units = pair ? sm_count / 2 : sm_count;  // concurrent tile workers
   const int bm = pair ? 2 * kBM : kBM;
   const int tiles_m = (M + bm - 1) / bm;

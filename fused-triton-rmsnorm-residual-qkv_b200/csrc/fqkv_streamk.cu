@@ -299,7 +299,7 @@ template <typename T, int MPAD>
 cudaError_t launch_t(const StreamKConfig& c, const CUtensorMap& tmW, const CUtensorMap& tmB,
                      const StreamKParams& p, bool pdl, cudaStream_t stream) {
   auto kern = streamk_kernel<T, MPAD>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), c.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

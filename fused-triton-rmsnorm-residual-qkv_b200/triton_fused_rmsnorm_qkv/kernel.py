@@ -27,6 +27,7 @@ streaming the weight before the preceding kernel in the stream has finished.
 """
 from __future__ import annotations
 
+import contextlib
 import os
 from typing import Optional, Tuple
 
@@ -37,15 +38,16 @@ from . import _lib
 # The reference switches kernels at M = 32 (kernel.py:360).  The B200 dispatch lives in
 # the C library; these mirror its bounds for readers of the Python API.
 _PERSISTENT_THRESHOLD = 32
-_DECODE_MAX_M = 32
-_SPLIT_MAX_M = 128
-
 _DTYPE_CODE = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
 _GAIN_CODE = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
 
 # (M, H) -> N of the last call, so get_autotune_best_config(M, H) can describe the
 # schedule the library chose for it (the reference reads Triton's autotune cache).
 _seen_shapes: dict[tuple[int, int], int] = {}
+
+# Workspace bytes per (M, H, N, dtype, schedule, device): the library's answer depends only
+# on these, and asking it every call costs a round trip through ctypes.
+_ws_bytes: dict[tuple, int] = {}
 
 
 def _env_flag(name: str) -> bool:
@@ -63,19 +65,37 @@ def _schedule_code(schedule) -> int:
     return int(schedule)
 
 
+def _current_stream(index: int) -> int:
+    """Handle of the current CUDA stream of device ``index`` (without building a Stream object)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return raw(index) if raw is not None else torch.cuda.current_stream(index).cuda_stream
+
+
 def _rows(t: torch.Tensor, M: int, H: int) -> torch.Tensor:
-    """View ``t`` as [M, H] with unit column stride (copying only if it must)."""
+    """``t`` (B, S, H) as M = B*S rows with one row stride and unit column stride.
+
+    The tensor is returned as it is when its rows already are uniformly strided (the
+    common case: no view is created); otherwise as an [M, H] view, or a copy if even that
+    is not possible."""
+    if t.dim() == 3 and t.stride(2) == 1 and (t.shape[0] == 1 or t.stride(0) == t.shape[1] * t.stride(1)):
+        return t
     t2 = t.reshape(M, H)
     if t2.stride(1) != 1:
         t2 = t2.contiguous()
     return t2
 
 
+def _row_stride(t: torch.Tensor) -> int:
+    return t.stride(-2) if t.dim() >= 2 else t.shape[-1]
+
+
 def _launch(x2: torch.Tensor, r2: Optional[torch.Tensor], rms_weight: torch.Tensor, weight: torch.Tensor,
             out2: torch.Tensor, rout2: Optional[torch.Tensor], eps: float, schedule: int,
-            static_weights: bool) -> None:
-    """Validate tensor metadata and call ``fqkv_launch`` on the current stream."""
-    M, H = x2.shape
+            static_weights: bool, M: int) -> None:
+    """Validate tensor metadata and call ``fqkv_launch`` on the current stream.  The
+    activation, output and residual-out tensors are M rows of H (N) elements with one row
+    stride each (see ``_rows``)."""
+    H = x2.shape[-1]
     N = weight.shape[0]
     if x2.dtype not in _DTYPE_CODE:
         raise TypeError(f"x must be float16 or bfloat16, got {x2.dtype}")
@@ -99,15 +119,19 @@ def _launch(x2: torch.Tensor, r2: Optional[torch.Tensor], rms_weight: torch.Tens
     flags = _lib.FLAG_PDL
     if static_weights:
         flags |= _lib.FLAG_STATIC_WEIGHTS
-    with torch.cuda.device(dev):
-        ws_bytes = _lib.workspace_bytes(M, H, N, _DTYPE_CODE[x2.dtype], code)
+    ctx = contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
+    with ctx:
+        key = (M, H, N, x2.dtype, code, dev.index)
+        ws_bytes = _ws_bytes.get(key)
+        if ws_bytes is None:
+            ws_bytes = _ws_bytes[key] = _lib.workspace_bytes(M, H, N, _DTYPE_CODE[x2.dtype], code)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
-        stream = torch.cuda.current_stream(dev).cuda_stream
+        stream = _current_stream(dev.index)
         rc = _lib.launch(
             x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), _GAIN_CODE[g.dtype],
             w.data_ptr(), out2.data_ptr(), rout2.data_ptr() if rout2 is not None else None,
-            M, H, N, x2.stride(0), r2.stride(0) if r2 is not None else 0, w.stride(0), out2.stride(0),
-            rout2.stride(0) if rout2 is not None else 0, float(eps), _DTYPE_CODE[x2.dtype], code, flags,
+            M, H, N, _row_stride(x2), _row_stride(r2) if r2 is not None else 0, w.stride(0), _row_stride(out2),
+            _row_stride(rout2) if rout2 is not None else 0, float(eps), _DTYPE_CODE[x2.dtype], code, flags,
             ws.data_ptr() if ws is not None else None, ws_bytes, stream)
     _lib.check(rc)
     _seen_shapes[(M, H)] = N
@@ -125,18 +149,18 @@ def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, stat
         if residual.numel() != M * H:
             raise ValueError(f"residual must match x {tuple(x.shape)}, got {tuple(residual.shape)}")
         r2 = _rows(residual, M, H)
-    out = torch.empty(M, N_OUT, dtype=x.dtype, device=x.device)
+    out = torch.empty(B, S, N_OUT, dtype=x.dtype, device=x.device)
     rout2 = None
     if residual_out is not None:
         if residual_out.numel() != M * H or residual_out.dtype != x.dtype or residual_out.device != x.device:
             raise ValueError("residual_out must have the shape, dtype and device of x")
-        rout2 = residual_out.view(M, H)
-        if rout2.stride(1) != 1:
-            raise ValueError("residual_out must have unit stride along H")
+        rout2 = _rows(residual_out, M, H)
+        if rout2.data_ptr() != residual_out.data_ptr() or rout2.stride(-1) != 1:
+            raise ValueError("residual_out must be writable as M rows with unit stride along H")
     if static_weights is None:
         static_weights = _env_flag("FQKV_STATIC_WEIGHTS")
-    _launch(x2, r2, rms_weight, weight, out, rout2, eps, schedule, static_weights)
-    return out.reshape(B, S, N_OUT)
+    _launch(x2, r2, rms_weight, weight, out, rout2, eps, schedule, static_weights, M)
+    return out
 
 
 def fused_rmsnorm_residual_matmul(
