@@ -20,7 +20,7 @@ namespace fqkv {
 // (CPT = ceil(H / 2048), so the register footprint, and hence occupancy, follows H).
 // ---------------------------------------------------------------------------
 template <typename T, int CPT>
-__global__ void __launch_bounds__(256) norm_prepass_kernel(const PrepassParams p) {
+__global__ void __launch_bounds__(256, CPT <= 2 ? 4 : 1) norm_prepass_kernel(const PrepassParams p) {
   constexpr int kMaxChunks = CPT;
   __shared__ float warp_sums[8];
   pdl_launch_dependents();
@@ -47,16 +47,19 @@ __global__ void __launch_bounds__(256) norm_prepass_kernel(const PrepassParams p
       load_gain8(p.g, p.gdt, (int64_t)c * 8, g[i]);
     }
   }
-  float ss = 0.f;
+  uint64_t ss2 = 0ull;
 #pragma unroll
   for (int i = 0; i < kMaxChunks; ++i) {
     const int c = tid + i * 256;
     if (c < nchunks) {
-      if (rrow) h[i] = add_rne8<T>(h[i], rv[i]);
-      ss = sumsq8_acc<T>(h[i], ss);
+      if (rrow) h[i] = add8_rn<T>(h[i], rv[i]);
+      ss2 = sumsq8_f2<T>(h[i], ss2);
       if (p.rout) *reinterpret_cast<uint4*>(p.rout + m * p.ldro + (int64_t)c * 8) = h[i];
     }
   }
+  float lo, hi;
+  f2_unpack(ss2, lo, hi);
+  float ss = lo + hi;
   // Block reduction in a fixed order (deterministic).
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -66,12 +69,17 @@ __global__ void __launch_bounds__(256) norm_prepass_kernel(const PrepassParams p
 #pragma unroll
   for (int w = 0; w < 8; ++w) total += warp_sums[w];
   const float rstd = row_rstd(total, p.H, p.eps);
+  const uint64_t rs2 = f2_pack(rstd, rstd);
 
   uint16_t* nrow = p.normed + m * p.H;
 #pragma unroll
   for (int i = 0; i < kMaxChunks; ++i) {
     const int c = tid + i * 256;
-    if (c < nchunks) *reinterpret_cast<uint4*>(nrow + (int64_t)c * 8) = normalize8g<T>(h[i], rstd, g[i]);
+    if (c < nchunks) {
+      const uint64_t g2[4] = {f2_pack(g[i][0].x, g[i][0].y), f2_pack(g[i][0].z, g[i][0].w),
+                              f2_pack(g[i][1].x, g[i][1].y), f2_pack(g[i][1].z, g[i][1].w)};
+      *reinterpret_cast<uint4*>(nrow + (int64_t)c * 8) = normalize8_f2<T>(h[i], rs2, g2);
+    }
   }
 }
 

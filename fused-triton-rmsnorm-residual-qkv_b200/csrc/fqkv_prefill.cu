@@ -271,8 +271,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      pdl_wait();  // A is written by the pre-pass
       const uint32_t half_bytes = L.stage_bytes;
+      // A static weight does not depend on the preceding grid: the weight halves of the
+      // first ring round go out before the pre-pass (which writes A) has finished.
+      int early = 0;
+      if ((p.flags & FQKV_FLAG_STATIC_WEIGHTS) && pair < tiles) {
+        const int nb0 = pair / p.tiles_m;
+        early = min(stages, KB);
+        for (int kb = 0; kb < early; ++kb) {
+          if (rank == 0) mbar_arrive_expect_tx(&full[kb], 2 * half_bytes);
+          tma_load_2d_pair(smem + kb * L.stage_bytes + kATileBytes, &tmB, mapa_shared(smem_u32(&full[kb]), 0),
+                           kb * kKBlock, nb0 * BN + (int)rank * (BN / 2));
+        }
+      }
+      pdl_wait();  // A is written by the pre-pass
       bool ok = true;
       int s = 0, round = 0, issued = 0;
       for (int t = pair; t < tiles && ok; t += npairs) {
@@ -280,12 +292,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < KB; ++kb) {
           if (round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1);
           if (!ok) break;
-          // The even CTA's full[s] counts both CTAs' bytes.
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * half_bytes);
           const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
           uint8_t* st = smem + s * L.stage_bytes;
+          if (issued >= early) {
+            // The even CTA's full[s] counts both CTAs' bytes.
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * half_bytes);
+            tma_load_2d_pair(st + kATileBytes, &tmB, bar, kb * kKBlock, nb * BN + (int)rank * (BN / 2));
+          }
           tma_load_2d_pair(st, &tmA, bar, kb * kKBlock, mb * 2 * kBM + (int)rank * kBM);
-          tma_load_2d_pair(st + kATileBytes, &tmB, bar, kb * kKBlock, nb * BN + (int)rank * (BN / 2));
           ++issued;
           if (++s == stages) {
             s = 0;
