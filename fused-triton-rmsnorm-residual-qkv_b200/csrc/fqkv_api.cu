@@ -448,13 +448,21 @@ extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const v
 
   GemmConfig g;
   if (int rc = gemm_pick_config((int)M, (int)H, (int)N, d.sms, &g)) return rc;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmO;
   if (int rc = make_map(&tmA, normed, M, H, H, 128, bf16)) return rc;
   if (int rc = make_map(&tmB, weight, N, H, ldw, g.pair ? g.bn / 2 : g.bn, bf16)) return rc;
+  // The CTA-pair kernel stores its tiles through a map of `out` (128 x 64 boxes) when the
+  // output's address and row pitch are 16-byte multiples.
+  const bool out_tma = g.pair && aligned16(out) && (ldo % 8) == 0;
+  if (out_tma) {
+    if (int rc = make_map(&tmO, out, M, N, ldo, 128, bf16)) return rc;
+  } else {
+    std::memset(&tmO, 0, sizeof(tmO));
+  }
   const int64_t bm = g.pair ? 256 : 128;
   GemmParams gp{static_cast<uint16_t*>(out), (int)M, (int)N, (int)H, ldo, (int)((H + 63) / 64),
-                (int)((M + bm - 1) / bm), (int)((N + g.bn - 1) / g.bn), flags};
-  e = launch_gemm(g, tmA, tmB, gp, bf16, true, st);
+                (int)((M + bm - 1) / bm), (int)((N + g.bn - 1) / g.bn), flags, out_tma ? 1 : 0};
+  e = launch_gemm(g, tmA, tmB, tmO, gp, bf16, true, st);
   return e == cudaSuccess ? 0 : cuda_fail(e, "prefill GEMM launch");
 }
 

@@ -74,6 +74,9 @@ struct GemmParams {
   int kb_total;
   int tiles_m, tiles_n;
   int flags;
+  // CTA-pair kernel: 1 when tmO maps `out` (16-byte aligned address and row pitch) and
+  // tiles leave through TMA tensor stores; 0 for per-thread stores.
+  int out_tma;
 };
 
 // ------------------------------------------------------------------ element helpers
@@ -337,7 +340,7 @@ struct GemmConfig {
   int pair;     // 1: 2-CTA clusters computing 256-row tiles (tcgen05 cta_group::2)
 };
 int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg);
-cudaError_t launch_gemm(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-                        bool bf16, bool pdl, cudaStream_t stream);
+cudaError_t launch_gemm(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                        const GemmParams& p, bool bf16, bool pdl, cudaStream_t stream);
 
 }  // namespace fqkv

@@ -28,14 +28,20 @@ constexpr int kBM = 128;
 constexpr int kKBlock = 64;
 constexpr int kATileBytes = kBM * 128;
 
+// Output staging of the CTA-pair kernel: two buffers of 128 rows x 64 columns (128 B
+// rows, 128-byte swizzle), each stored by one TMA tensor store.
+constexpr uint32_t kOutChunkBytes = kBM * 128;
+constexpr uint32_t kOutStageBytes = 2 * kOutChunkBytes;
+
 struct GLayout {
-  uint32_t stage_bytes, bars, tmem_slot, total;
+  uint32_t stage_bytes, stage_out, bars, tmem_slot, total;
 };
 
-__host__ __device__ inline GLayout make_glayout(int stages, int bn) {
+__host__ __device__ inline GLayout make_glayout(int stages, int bn, uint32_t out_bytes = 0) {
   GLayout L;
-  L.stage_bytes = kATileBytes + bn * 128;
-  L.bars = stages * L.stage_bytes;                 // full[S], empty[S], tfull[2], tempty[2], done
+  L.stage_bytes = kATileBytes + bn * 128;          // a multiple of 1024
+  L.stage_out = stages * L.stage_bytes;            // output staging, 1024-aligned
+  L.bars = L.stage_out + out_bytes;                // full[S], empty[S], tfull[2], tempty[2], done
   L.tmem_slot = L.bars + (2 * stages + 5) * 8;
   L.total = L.tmem_slot + 16;
   return L;
@@ -50,6 +56,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+
+// Wait for this thread's TMEM loads.  The loaded registers pass through empty asm
+// statements after the wait, so no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&a)[32], uint32_t (&b)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(a[i]), "+r"(b[i]));
 }
 
 template <typename T, int BN>
@@ -221,13 +235,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   tfull[b]  (each CTA) accumulator b ready: one commit multicast to both CTAs;
 //   tempty[b] (even CTA) accumulator b drained: one arrive per epilogue warp of both CTAs;
 //   done      (each CTA) every MMA retired (multicast), before TMEM is freed.
+// Epilogue: each CTA converts its 128 rows 64 columns at a time into a 128B-swizzled
+// staging buffer (two, alternating) and one thread stores the 128 x 64 box with a TMA
+// tensor store, when `out` allows a tensor map (p.out_tma); otherwise every thread
+// stores its row.
 template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmParams p, const int stages) {
+                     const __grid_constant__ CUtensorMap tmO, const GemmParams p, const int stages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const GLayout L = make_glayout(stages, BN / 2);
+  const GLayout L = make_glayout(stages, BN / 2, kOutStageBytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
@@ -257,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.out_tma) tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -354,6 +373,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0) && ((p.ldo & 7) == 0);
     const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const int row = q * 32 + lane;  // this thread's row of the CTA's 128-row half
+    uint8_t* const stage_out = smem + L.stage_out;
+    const bool issuer = row == 0;  // issues and tracks this CTA's output TMA stores
+    int n_out = 0;                 // output chunks staged so far (buffer n_out & 1 is next)
     bool ok = true;
     int li = 0;
     for (int t = pair; t < tiles && ok; t += npairs, ++li) {
@@ -362,7 +385,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int mb = t % p.tiles_m, nb = t / p.tiles_m;
-      const int64_t m = (int64_t)mb * 2 * kBM + (int64_t)rank * kBM + q * 32 + lane;
+      if (p.out_tma) {
+        // TMEM -> registers (64 columns per wait) -> dtype -> staging buffer -> one TMA
+        // store per 128 x 64 box.  Rows at or beyond M and columns at or beyond N lie
+        // outside the tensor map and are not written.
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+        const int m0 = mb * 2 * kBM + (int)rank * kBM;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+          uint32_t va[32], vb[32];
+          tmem_ld32(tbase + c0, va);
+          tmem_ld32(tbase + c0 + 32, vb);
+          tmem_wait_ld_regs(va, vb);
+          if (c0 + 64 >= BN) {  // the accumulator is drained: the MMA may reuse it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(tempty0 + buf * 8);
+          }
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            pk[e] = Elem<T>::from_f2(__uint_as_float(va[2 * e]), __uint_as_float(va[2 * e + 1]));
+            pk[16 + e] = Elem<T>::from_f2(__uint_as_float(vb[2 * e]), __uint_as_float(vb[2 * e + 1]));
+          }
+          uint8_t* sbuf = stage_out + (n_out & 1) * kOutChunkBytes;
+          if (n_out >= 2) {  // the store issued from this buffer two chunks ago has read it
+            if (issuer) bulk_wait_group_read<1>();
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+          }
+          // 16-byte chunk j of a 128-byte row sits at j ^ (row % 8): the 128-byte swizzle.
+          uint8_t* srow = sbuf + row * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(srow + ((j ^ (row & 7)) << 4)) =
+                make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          fence_proxy_async_smem();  // the staged tile is visible to the TMA unit
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          if (issuer && m0 < p.M && nb * BN + c0 < p.N) {
+            tma_store_2d(&tmO, sbuf, nb * BN + c0, m0);
+            bulk_commit_group();
+          }
+          ++n_out;
+        }
+        continue;
+      }
+      const int64_t m = (int64_t)mb * 2 * kBM + (int64_t)rank * kBM + row;
       uint16_t* orow = p.out + m * p.ldo;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -390,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty0 + buf * 8);
     }
+    if (issuer) bulk_wait_group<0>();  // every output store has completed
   }
 
   // ---------------------------------------------------------------- teardown
@@ -403,8 +471,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <typename T, int BN>
-cudaError_t launch_pair_bn(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-                           bool pdl, cudaStream_t stream) {
+cudaError_t launch_pair_bn(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                           const GemmParams& p, bool pdl, cudaStream_t stream) {
   auto kern = gemm_pair_kernel<T, BN>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), c.smem);
   if (e != cudaSuccess) return e;
@@ -426,7 +494,7 @@ cudaError_t launch_pair_bn(const GemmConfig& c, const CUtensorMap& tmA, const CU
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p, c.stages);
+  return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, p, c.stages);
 }
 
 template <typename T, int BN>
@@ -453,12 +521,12 @@ cudaError_t launch_bn(const GemmConfig& c, const CUtensorMap& tmA, const CUtenso
 }
 
 template <typename T>
-cudaError_t launch_t(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-                     bool pdl, cudaStream_t stream) {
+cudaError_t launch_t(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                     const GemmParams& p, bool pdl, cudaStream_t stream) {
   if (c.pair) {
     switch (c.bn) {
-      case 128: return launch_pair_bn<T, 128>(c, tmA, tmB, p, pdl, stream);
-      case 256: return launch_pair_bn<T, 256>(c, tmA, tmB, p, pdl, stream);
+      case 128: return launch_pair_bn<T, 128>(c, tmA, tmB, tmO, p, pdl, stream);
+      case 256: return launch_pair_bn<T, 256>(c, tmA, tmB, tmO, p, pdl, stream);
       default: return cudaErrorInvalidValue;
     }
   }
@@ -474,21 +542,27 @@ cudaError_t launch_t(const GemmConfig& c, const CUtensorMap& tmA, const CUtensor
 
 constexpr size_t kGemmSmemLimit = 232448;
 
-// Tile width BN: the candidate with the fewest "tile-waves x (BN + A share)" (time proxy
-// with one CTA per SM), ties going to the wider tile; ring depth as deep as shared memory
-// allows.  FQKV_GEMM_BN restricts the choice.
+// Kernel and tile width, from measurements on B200 at H = 4096, N = 6144 (graph-timed
+// prefill, M = 512 ... 8192):
+//   - CTA pairs with 256 x 256 tiles are the fastest kernel above 512 rows (M = 1024:
+//     55 us against 57 us for the best single-CTA tile; M = 2048: 85 against 92 us);
+//     at M <= 512 the single-CTA kernel fills more SMs and ties or wins.
+//   - A 256 x 128 pair tile takes ~93% of the time of a 256 x 256 one, so pairs use
+//     BN = 128 only when N <= 128.
+//   - Single-CTA tiles: the fewest "tile-waves x (BN + 300)" (a wave of 128 x BN tiles
+//     costs about BN + 300 in these units), ties going to the wider tile.
+// FQKV_GEMM_PAIR=0 / 1 and FQKV_GEMM_BN override the choice (read once per process).
 int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg) {
   (void)H;
-  static const int force_bn = [] {  // tuning overrides, read once per process
+  static const int force_bn = [] {
     const char* v = std::getenv("FQKV_GEMM_BN");
     return (v && *v) ? std::atoi(v) : 0;
   }();
-  // CTA pairs (256-row tiles) for M > 128 unless FQKV_GEMM_PAIR=0.
-  static const bool pair_allowed = [] {
+  static const int force_pair = [] {  // -1: automatic
     const char* v = std::getenv("FQKV_GEMM_PAIR");
-    return !(v && *v) || std::atoi(v) != 0;
+    return (v && *v) ? (std::atoi(v) != 0 ? 1 : 0) : -1;
   }();
-  const bool pair = M > kBM && pair_allowed;
+  const bool pair = M > kBM && (force_pair >= 0 ? force_pair == 1 : M > 4 * kBM);
   const int units = pair ? sm_count / 2 : sm_count;  // concurrent tile workers
   const int bm = pair ? 2 * kBM : kBM;
   const int tiles_m = (M + bm - 1) / bm;
@@ -499,12 +573,10 @@ int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg) {
     // 256 x 192 pair tiles (96 B rows per CTA) measured 2-3x slower than 256 x 256 on
     // B200, and their results are not covered by the tests: pairs use 256 or 128.
     if (pair && bn == 192) continue;
+    if (pair && bn == 128 && N > 128 && !force_bn) continue;
     const long tiles = (long)tiles_m * ((N + bn - 1) / bn);
     const long waves = (tiles + units - 1) / units;
-    // A tile-wave costs its width plus a fixed share for the A operand, which every tile
-    // reloads whatever its width (measured on B200: at M = 2048 / 8192, BN = 256 beats the
-    // narrower tiles although they fill the last wave better).
-    const long cost = waves * (bn + 96);
+    const long cost = waves * (bn + 300);
     if (best_bn == 0 || cost < best_cost) {
       best_bn = bn;
       best_cost = cost;
@@ -516,18 +588,19 @@ int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg) {
   c.pair = pair ? 1 : 0;
   const int b_rows = pair ? c.bn / 2 : c.bn;  // B rows each CTA loads per stage
   c.stages = 2;
-  while (c.stages < 8 && 1024 + make_glayout(c.stages + 1, b_rows).total <= kGemmSmemLimit) ++c.stages;
-  c.smem = 1024 + make_glayout(c.stages, b_rows).total;
+  const uint32_t out_bytes = pair ? kOutStageBytes : 0;  // output staging of the pair kernel
+  while (c.stages < 8 && 1024 + make_glayout(c.stages + 1, b_rows, out_bytes).total <= kGemmSmemLimit) ++c.stages;
+  c.smem = 1024 + make_glayout(c.stages, b_rows, out_bytes).total;
   const long tiles = (long)tiles_m * ((N + c.bn - 1) / c.bn);
   c.grid = (int)(tiles < units ? tiles : units) * (pair ? 2 : 1);
   *cfg = c;
   return 0;
 }
 
-cudaError_t launch_gemm(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-                        bool bf16, bool pdl, cudaStream_t stream) {
-  return bf16 ? launch_t<__nv_bfloat16>(c, tmA, tmB, p, pdl, stream)
-              : launch_t<__half>(c, tmA, tmB, p, pdl, stream);
+cudaError_t launch_gemm(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                        const GemmParams& p, bool bf16, bool pdl, cudaStream_t stream) {
+  return bf16 ? launch_t<__nv_bfloat16>(c, tmA, tmB, tmO, p, pdl, stream)
+              : launch_t<__half>(c, tmA, tmB, tmO, p, pdl, stream);
 }
 
 }  // namespace fqkv

@@ -116,7 +116,9 @@ SCHEDULE_CASES = [
     (100, 520, 392, ("simt", "split", "prefill")),
     (128, 1024, 1536, ("simt", "split", "prefill")),
     (129, 768, 1000, ("simt", "prefill")),
-    (777, 1024, 1280, ("simt", "prefill")),
+    (777, 1024, 1280, ("simt", "prefill")),    # CTA-pair kernel, ragged M
+    (600, 512, 128, ("simt", "prefill")),      # CTA pairs with 256 x 128 tiles (N <= 128)
+    (1100, 256, 72, ("prefill",)),             # the same, one 64-column box clipped at N
 ]
 
 
@@ -126,6 +128,39 @@ SCHEDULE_CASES = [
 def test_every_schedule(M, H, N, scheds, dtype, res):
     for s in scheds:
         run_case(M, H, N, dtype, seed=M * 7 + H, res=res, schedule=s)
+
+
+@pytest.mark.parametrize("M,H,N", [(777, 1024, 1280), (600, 512, 128), (300, 1024, 1280)])
+@pytest.mark.parametrize("pad,offset", [(8, 0), (3, 1)], ids=["pitch16B", "unaligned"])
+def test_prefill_output_rows_in_a_wider_buffer(M, H, N, pad, offset):
+    """The prefill GEMM writes its M x N tile into rows of a wider buffer (row pitch N + pad)
+    through the C ABI.  A 16-byte aligned address and pitch lets the CTA-pair kernel store
+    through a tensor map (clipped at N); an odd pitch or address makes it store rows per
+    thread.  Either way the results match the oracle and nothing outside the M x N block
+    is written."""
+    x, r, g, w = make_case(M, H, N, torch.bfloat16, 41 + pad)
+    dev = "cuda"
+    xd, rd, gd, wd = (t.to(dev) for t in (x, r, g, w))
+    ldo = N + pad
+    buf = torch.full((offset + M * ldo + 8,), float("nan"), dtype=torch.bfloat16, device=dev)
+    out = buf[offset:offset + M * ldo].view(M, ldo)
+    hidden = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    code = _lib.SCHED_PREFILL
+    ws_bytes = _lib.workspace_bytes(M, H, N, _lib.BF16, code)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    rc = _lib.launch(xd.data_ptr(), rd.data_ptr(), gd.data_ptr(), _lib.BF16, wd.data_ptr(), out.data_ptr(),
+                     hidden.data_ptr(), M, H, N, H, H, H, ldo, H, 1e-5, _lib.BF16, code, _lib.FLAG_PDL,
+                     ws.data_ptr(), ws_bytes, torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc)
+    torch.cuda.synchronize()
+    ref_out, ref_hidden = forward(x, r, g, w, 1e-5)
+    got = out[:, :N].cpu()
+    m = parity_metrics(got, ref_out)
+    assert within_bars(m, MAX_ABS, REL_L2), m
+    assert torch.equal(hidden.cpu(), ref_hidden)
+    assert torch.isnan(out[:, N:].float()).all(), "the GEMM wrote past column N"
+    assert torch.isnan(buf[:offset].float()).all() and torch.isnan(buf[offset + M * ldo:].float()).all()
+    assert _lib_status_clear()
 
 
 @pytest.mark.parametrize("M,H", [(3, 100), (17, 250), (40, 4100)])
