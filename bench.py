@@ -535,14 +535,28 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
                "sample": f"{n} ops of the same workload (M={M}, H={H}, N={N_glob}, bf16, one seeded set) "
                          f"over ~{args.cpu_seconds:.0f} s, median op time {sec * 1e3:.3f} ms"}
 
-    achieved = per_rank / step_s / 1e9
-    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / peaks["hbm_gbs"], 4),
-            "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)",
-            "pct_of_8TBs_spec": round(100 * achieved / HBM_SPEC_GBS, 2),
-            "traffic": profile_traffic(f"decode_llama3-8b_m{M}"),
-            "kernel": "decode_kernel (fused swap-AB tcgen05, cluster split-K)" if not sched["uses_prepass"]
-            else "norm_prepass_kernel + decode_kernel"}
+    if sched["schedule"] == _lib.SCHED_PREFILL:
+        # Tensor-bound: FLOPs of the step over its time (pre-pass + GEMM), against the
+        # measured cuBLAS bf16 burst peak.
+        gemm = "gemm_pair_kernel (2-CTA tcgen05)" if sched["block_m"] == 256 else "gemm_kernel (tcgen05)"
+        achieved = 2.0 * M * N_loc * H / step_s / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)",
+                "traffic": profile_traffic(f"prefill_gemm_pair_llama3-8b_m{M}"),
+                "kernel": f"norm_prepass_kernel + {gemm}; time of the whole step"}
+    else:
+        achieved = per_rank / step_s / 1e9
+        kernel = {_lib.SCHED_DECODE: "decode_kernel (fused swap-AB tcgen05, cluster split-K)",
+                  _lib.SCHED_SPLIT: "norm_prepass_kernel + streamk_kernel; time of the whole step"}.get(
+                      sched["schedule"], "simt_kernel")
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)",
+                "pct_of_8TBs_spec": round(100 * achieved / HBM_SPEC_GBS, 2),
+                "traffic": profile_traffic(f"decode_llama3-8b_m{M}") if sched["schedule"] == _lib.SCHED_DECODE
+                else None,
+                "kernel": kernel}
 
     line = {
         "metric": METRIC,
