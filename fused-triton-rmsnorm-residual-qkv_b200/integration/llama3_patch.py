@@ -14,6 +14,13 @@ Same public surface and behaviour as the reference's ``integration/llama3_patch.
   (llama3_patch.py:61-65);
 * ``remove_fused_patch`` / ``fused_patch`` undo it (llama3_patch.py:218-239).
 
+Beyond the reference, ``apply_fused_patch(model, mlp=True)`` also routes the layer's
+second half through the op.  ``fused_add_rmsnorm_matmul(attn_out, residual,
+post_attention_layernorm.weight, [W_gate; W_up])`` forms the updated residual stream
+``residual + attn_out`` (bit-exact, returned), normalises it and projects it onto the
+packed gate/up weight in one launch.  The layer then applies ``down_proj(act(gate) * up)``
+and adds the MLP output to the returned stream (llama3_patch.py:190-194).
+
 Written against transformers 5.5 (``LlamaDecoderLayer.forward`` / ``LlamaAttention``).
 """
 from __future__ import annotations
@@ -31,7 +38,11 @@ from transformers.models.llama.modeling_llama import (
     eager_attention_forward,
 )
 
-from triton_fused_rmsnorm_qkv import fused_rmsnorm_residual_matmul, fused_rmsnorm_residual_matmul_fixed
+from triton_fused_rmsnorm_qkv import (
+    fused_add_rmsnorm_matmul,
+    fused_rmsnorm_residual_matmul,
+    fused_rmsnorm_residual_matmul_fixed,
+)
 
 LLAMA3_8B_CONFIG = dict(
     hidden_size=4096,
@@ -50,6 +61,7 @@ LLAMA3_8B_CONFIG = dict(
 )
 
 _ORIGINAL = "_fused_original_forward"
+_LAYER_ATTRS = ("_fused_packed_qkv", "_fused_H_kv", "_fused_packed_gate_up", "_fused_intermediate")
 
 
 def _fused_op():
@@ -86,9 +98,21 @@ def pack_qkv_weight(attn: LlamaAttention) -> torch.Tensor:
     return torch.cat([wq.detach(), wk.detach(), wv.detach()], dim=0).contiguous()
 
 
+def pack_gate_up_weight(mlp) -> torch.Tensor:
+    """``[W_gate; W_up]`` stacked along the output dimension (2 * intermediate rows)."""
+    wg, wu = mlp.gate_proj.weight, mlp.up_proj.weight
+    if wg.shape != wu.shape:
+        raise ValueError(f"gate_proj {tuple(wg.shape)} and up_proj {tuple(wu.shape)} must have the same shape")
+    if getattr(mlp.gate_proj, "bias", None) is not None or getattr(mlp.up_proj, "bias", None) is not None:
+        raise ValueError("the fused gate/up projection has no bias")
+    return torch.cat([wg.detach(), wu.detach()], dim=0).contiguous()
+
+
 def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
                      use_cache=False, position_embeddings=None, **kwargs):
-    """LlamaDecoderLayer.forward with input_layernorm + q/k/v_proj replaced by one fused op."""
+    """LlamaDecoderLayer.forward with input_layernorm + q/k/v_proj replaced by one fused op
+    (and, when the layer was patched with ``mlp=True``, the post-attention residual add +
+    post_attention_layernorm + gate/up projections by a second one)."""
     attn = self.self_attn
     lead = hidden_states.shape[:-1]
     h_kv = self._fused_H_kv
@@ -105,17 +129,30 @@ def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None
         k, v = past_key_values.update(k, v, attn.layer_idx)
     attend = ALL_ATTENTION_FUNCTIONS.get_interface(attn.config._attn_implementation, eager_attention_forward)
     ctx, _ = attend(attn, q, k, v, attention_mask, dropout=0.0, scaling=attn.scaling, **kwargs)
-    hidden_states = hidden_states + attn.o_proj(ctx.reshape(*lead, -1).contiguous())
-    return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
+    attn_out = attn.o_proj(ctx.reshape(*lead, -1).contiguous())
+    gate_up_w = getattr(self, "_fused_packed_gate_up", None)
+    if gate_up_w is None:
+        hidden_states = hidden_states + attn_out
+        return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
+    post = self.post_attention_layernorm
+    fixed = os.environ.get("TRITON_FUSED_DISABLE_AUTOTUNE") == "1"  # the _fixed path's kernel
+    gate_up, hidden_states = fused_add_rmsnorm_matmul(attn_out, hidden_states, post.weight, gate_up_w,
+                                                      eps=post.variance_epsilon, schedule="simt" if fixed else None)
+    gate, up = torch.split(gate_up, [self._fused_intermediate, self._fused_intermediate], dim=-1)
+    return hidden_states + self.mlp.down_proj(self.mlp.act_fn(gate) * up)
 
 
-def apply_fused_patch(model: LlamaForCausalLM) -> LlamaForCausalLM:
-    """Patch every decoder layer of ``model`` (idempotent)."""
+def apply_fused_patch(model: LlamaForCausalLM, *, mlp: bool = False) -> LlamaForCausalLM:
+    """Patch every decoder layer of ``model`` (idempotent).  ``mlp=True`` also fuses the
+    post-attention residual add + norm + gate/up projections."""
     for layer in model.model.layers:
         if hasattr(layer, _ORIGINAL):
             continue
         layer._fused_packed_qkv = pack_qkv_weight(layer.self_attn)
         layer._fused_H_kv = layer.self_attn.k_proj.weight.shape[0]
+        if mlp:
+            layer._fused_packed_gate_up = pack_gate_up_weight(layer.mlp)
+            layer._fused_intermediate = layer.mlp.gate_proj.weight.shape[0]
         setattr(layer, _ORIGINAL, layer.forward)
         layer.forward = _patched_forward.__get__(layer, type(layer))
     return model
@@ -128,16 +165,16 @@ def remove_fused_patch(model: LlamaForCausalLM) -> LlamaForCausalLM:
             continue
         layer.forward = getattr(layer, _ORIGINAL)
         delattr(layer, _ORIGINAL)
-        for name in ("_fused_packed_qkv", "_fused_H_kv"):
+        for name in _LAYER_ATTRS:
             if hasattr(layer, name):
                 delattr(layer, name)
     return model
 
 
 @contextmanager
-def fused_patch(model: LlamaForCausalLM):
+def fused_patch(model: LlamaForCausalLM, *, mlp: bool = False):
     """Apply the patch for the duration of a ``with`` block."""
-    apply_fused_patch(model)
+    apply_fused_patch(model, mlp=mlp)
     try:
         yield model
     finally:

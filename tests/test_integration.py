@@ -7,7 +7,7 @@ import torch
 from transformers import LlamaConfig, LlamaForCausalLM
 
 from integration import LLAMA3_8B_CONFIG, apply_fused_patch, build_llama3_8b, fused_patch, remove_fused_patch
-from integration.llama3_patch import pack_qkv_weight
+from integration.llama3_patch import pack_gate_up_weight, pack_qkv_weight
 
 
 def tiny_llama(device="cpu", dtype=torch.float32, layers=2):
@@ -50,39 +50,82 @@ def test_patch_and_unpatch_bookkeeping():
     assert not any(hasattr(layer, "_fused_packed_qkv") for layer in model.model.layers)
 
 
+def test_pack_gate_up_is_gate_then_up():
+    model = tiny_llama()
+    mlp = model.model.layers[1].mlp
+    packed = pack_gate_up_weight(mlp)
+    assert packed.shape == (2 * 512, 256)
+    assert torch.equal(packed[:512], mlp.gate_proj.weight)
+    assert torch.equal(packed[512:], mlp.up_proj.weight)
+
+
+def test_mlp_patch_bookkeeping():
+    model = tiny_llama()
+    originals = [layer.forward for layer in model.model.layers]
+    with fused_patch(model, mlp=True):
+        for layer in model.model.layers:
+            assert layer._fused_packed_gate_up.shape == (1024, 256) and layer._fused_intermediate == 512
+            assert hasattr(layer, "_fused_packed_qkv")
+    for layer, fwd in zip(model.model.layers, originals):
+        assert not hasattr(layer, "_fused_packed_gate_up") and not hasattr(layer, "_fused_intermediate")
+        assert layer.forward == fwd
+    apply_fused_patch(model)  # the reference's default: Q/K/V only
+    assert not any(hasattr(layer, "_fused_packed_gate_up") for layer in model.model.layers)
+    remove_fused_patch(model)
+
+
 def test_llama3_8b_config_shape():
     assert LLAMA3_8B_CONFIG["hidden_size"] + 2 * LLAMA3_8B_CONFIG["num_key_value_heads"] * \
         LLAMA3_8B_CONFIG["head_dim"] == 6144
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("mlp", [False, True], ids=["qkv", "qkv+mlp"])
 @pytest.mark.parametrize("fixed", [False, True], ids=["auto", "fixed"])
-def test_patched_tiny_llama_matches_unpatched(fixed, monkeypatch):
+def test_patched_tiny_llama_matches_unpatched(fixed, mlp, monkeypatch):
     if fixed:
         monkeypatch.setenv("TRITON_FUSED_DISABLE_AUTOTUNE", "1")
     model = tiny_llama("cuda", torch.bfloat16)
     ids = torch.randint(0, 500, (2, 24), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
     with torch.no_grad():
         ref = model(ids).logits.float()
-        with fused_patch(model):
+        with fused_patch(model, mlp=mlp):
             got = model(ids).logits.float()
     rel = (got - ref).norm() / ref.norm()
     assert rel < 2e-2, float(rel)
 
 
+def _prefill_then_decode(model, ids, cont):
+    """Last-position logits of a prefill of ``ids`` and then one decode step per token of
+    ``cont`` through the KV cache (teacher forcing: both runs see the same tokens)."""
+    out = model(ids, use_cache=True)
+    logits, cache = [out.logits[:, -1].float()], out.past_key_values
+    for j in range(cont.shape[1]):
+        out = model(cont[:, j:j + 1], past_key_values=cache, use_cache=True)
+        logits.append(out.logits[:, -1].float())
+        cache = out.past_key_values
+    return logits
+
+
 @pytest.mark.gpu
-def test_patched_llama3_8b_two_layers_decode_and_prefill():
-    """The Llama-3-8B layer shape (2 layers): prefill of 32 tokens, then 4 greedy decode
-    steps through the KV cache, patched vs unpatched."""
+@pytest.mark.parametrize("mlp", [False, True], ids=["qkv", "qkv+mlp"])
+def test_patched_llama3_8b_two_layers_decode_and_prefill(mlp):
+    """The Llama-3-8B layer shape (2 layers): prefill of 32 tokens (M = 32), then 4 decode
+    steps (M = 1) through the KV cache, patched vs unpatched on the same token sequence.
+    With ``mlp`` the post-attention add + norm + gate/up (N = 2 x 14336) runs through the
+    fused op too.  (Greedy generation is not compared: with random weights the logits are
+    nearly flat, and a rounding-level difference can change the argmax and so every later
+    step's input.)"""
     model = build_llama3_8b(dtype=torch.bfloat16, device="cuda", num_hidden_layers=2)
-    ids = torch.randint(0, 128256, (1, 32), device="cuda", generator=torch.Generator(device="cuda").manual_seed(2))
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    ids = torch.randint(0, 128256, (1, 32), device="cuda", generator=gen)
+    cont = torch.randint(0, 128256, (1, 4), device="cuda", generator=gen)
     with torch.no_grad():
-        ref = model.generate(ids, max_new_tokens=4, do_sample=False, output_logits=True, return_dict_in_generate=True)
-        with fused_patch(model):
-            got = model.generate(ids, max_new_tokens=4, do_sample=False, output_logits=True,
-                                 return_dict_in_generate=True)
-    for a, b in zip(got.logits, ref.logits):
-        rel = (a.float() - b.float()).norm() / b.float().norm()
+        ref = _prefill_then_decode(model, ids, cont)
+        with fused_patch(model, mlp=mlp):
+            got = _prefill_then_decode(model, ids, cont)
+    for a, b in zip(got, ref):
+        rel = (a - b).norm() / b.norm()
         assert rel < 3e-2, float(rel)
     del model
     torch.cuda.empty_cache()
