@@ -22,7 +22,9 @@ residual add with the updated residual returned).  32 distinct seeded weight set
              (bf16, fp16), Qwen2-7B decode M=1/16/64 (with and without residual),
              Llama-3-70B M=1/16/256, the post-attention gate/up shape (N=28672), prefill
              M=512/2048/8192 (TFLOPS), the unfused PyTorch path (cuBLAS) on the same
-             inputs as the GPU comparator, and a streaming-read bandwidth for context.
+             inputs as the GPU comparator, a streaming-read bandwidth for context, and
+             a 4-layer Llama-3-8B stack (M=1/16) unpatched vs the integration patch's
+             three modes (Q/K/V, + MLP gate/up, cross-layer).
 With N > 1 (torchrun) the layer is head-sharded column-parallel: each rank owns N/P
 weight rows and computes them with replicated inputs; no collective runs inside the
 timed region.  After timing, an NCCL all-gather reassembles one step for a check
@@ -392,7 +394,45 @@ def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
             entry["speedup_vs_torch_unfused"] = round(t_ref / t_ms, 2)
         detail[label] = entry
         del ss
+    detail["llama3-8b_layer_stack"] = run_layer_stack(dev)
     return detail
+
+
+def run_layer_stack(dev, n_layers: int = 4, ms=(1, 16), steps: int = 50) -> dict:
+    """Model-level check of the integration: a stack of Llama-3-8B decoder layers (random
+    init, bf16, no KV cache, causal attention over the M tokens) and the final norm,
+    graph-timed per forward of M tokens.  Unpatched PyTorch against the patch in its three
+    modes: Q/K/V only (the reference's patch), + post-attention add/norm/gate-up, and
+    cross-layer (each layer's MLP residual add fused into the next layer's input call)."""
+    from contextlib import nullcontext
+
+    from integration import build_llama3_8b, fused_patch
+
+    model = build_llama3_8b(dtype=torch.bfloat16, device=str(dev), num_hidden_layers=n_layers)
+    inner = model.model
+    modes = (("unpatched", None), ("qkv", {}), ("qkv+mlp", {"mlp": True}), ("cross-layer", {"cross_layer": True}))
+    out = {"layers": n_layers, "steps": steps, "unit": "us per forward of M tokens through all layers"}
+    with torch.no_grad():
+        for M in ms:
+            gen = torch.Generator(device=dev).manual_seed(5)
+            h0 = torch.randn(1, M, WORKLOADS["llama3-8b-decode"]["H"], generator=gen, device=dev, dtype=torch.bfloat16)
+            pos = torch.arange(M, device=dev)[None]
+            pe = inner.rotary_emb(h0, pos)
+
+            def step(i):
+                x = h0
+                for layer in inner.layers:
+                    x = layer(x, attention_mask=None, position_ids=pos, position_embeddings=pe)
+                return inner.norm(x)
+
+            row = {}
+            for name, kw in modes:
+                with (nullcontext() if kw is None else fused_patch(model, **kw)):
+                    row[name] = round(time_graph(step, steps, 3, dev) / steps * 1e3, 2)
+            out[f"M{M}"] = row
+    del model, inner
+    torch.cuda.empty_cache()
+    return out
 
 
 # ----------------------------------------------------------------------------- GPU arm

@@ -21,6 +21,14 @@ post_attention_layernorm.weight, [W_gate; W_up])`` forms the updated residual st
 packed gate/up weight in one launch.  The layer then applies ``down_proj(act(gate) * up)``
 and adds the MLP output to the returned stream (llama3_patch.py:190-194).
 
+``cross_layer=True`` (implies ``mlp=True``) also fuses across layer boundaries.  A layer
+other than the last returns its MLP output alone and leaves the updated residual stream
+in a per-model carry.  The next layer's input call is then
+``fused_add_rmsnorm_matmul(mlp_out, stream, input_layernorm.weight, [Wq; Wk; Wv])``: one
+launch adds the two (bit-exact), normalises and projects.  The last layer returns the
+full stream, so the final norm is unchanged.  With it, hidden states collected between
+layers (``output_hidden_states``) are the MLP outputs, not the stream.
+
 Written against transformers 5.5 (``LlamaDecoderLayer.forward`` / ``LlamaAttention``).
 """
 from __future__ import annotations
@@ -61,14 +69,23 @@ LLAMA3_8B_CONFIG = dict(
 )
 
 _ORIGINAL = "_fused_original_forward"
-_LAYER_ATTRS = ("_fused_packed_qkv", "_fused_H_kv", "_fused_packed_gate_up", "_fused_intermediate")
+_LAYER_ATTRS = ("_fused_packed_qkv", "_fused_H_kv", "_fused_packed_gate_up", "_fused_intermediate",
+                "_fused_carry", "_fused_first", "_fused_last")
+
+
+def _fixed() -> bool:
+    """TRITON_FUSED_DISABLE_AUTOTUNE=1 selects the fixed-tile (``_fixed``) kernels."""
+    return os.environ.get("TRITON_FUSED_DISABLE_AUTOTUNE") == "1"
 
 
 def _fused_op():
     """The fused entry point for this call (env TRITON_FUSED_DISABLE_AUTOTUNE=1 -> _fixed)."""
-    if os.environ.get("TRITON_FUSED_DISABLE_AUTOTUNE") == "1":
-        return fused_rmsnorm_residual_matmul_fixed
-    return fused_rmsnorm_residual_matmul
+    return fused_rmsnorm_residual_matmul_fixed if _fixed() else fused_rmsnorm_residual_matmul
+
+
+def _fused_add(x, residual, rms_weight, weight, eps):
+    """(out, x + residual) in one launch, on the fixed-tile kernel when _fixed()."""
+    return fused_add_rmsnorm_matmul(x, residual, rms_weight, weight, eps=eps, schedule="simt" if _fixed() else None)
 
 
 def build_llama3_8b(dtype: torch.dtype = torch.float16, device: str = "cuda",
@@ -117,8 +134,15 @@ def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None
     lead = hidden_states.shape[:-1]
     h_kv = self._fused_H_kv
     h_q = self._fused_packed_qkv.shape[0] - 2 * h_kv
-    qkv = _fused_op()(hidden_states, None, self.input_layernorm.weight, self._fused_packed_qkv,
-                      eps=self.input_layernorm.variance_epsilon)
+    carry = getattr(self, "_fused_carry", None)
+    pending = None if carry is None or self._fused_first else carry.pop("stream", None)
+    if pending is None:
+        qkv = _fused_op()(hidden_states, None, self.input_layernorm.weight, self._fused_packed_qkv,
+                          eps=self.input_layernorm.variance_epsilon)
+    else:
+        # The previous layer's MLP output arrives with the stream it belongs to.
+        qkv, hidden_states = _fused_add(hidden_states, pending, self.input_layernorm.weight, self._fused_packed_qkv,
+                                        self.input_layernorm.variance_epsilon)
     q, k, v = torch.split(qkv, [h_q, h_kv, h_kv], dim=-1)
     q = q.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
     k = k.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
@@ -135,17 +159,25 @@ def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None
         hidden_states = hidden_states + attn_out
         return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
     post = self.post_attention_layernorm
-    fixed = os.environ.get("TRITON_FUSED_DISABLE_AUTOTUNE") == "1"  # the _fixed path's kernel
-    gate_up, hidden_states = fused_add_rmsnorm_matmul(attn_out, hidden_states, post.weight, gate_up_w,
-                                                      eps=post.variance_epsilon, schedule="simt" if fixed else None)
+    gate_up, hidden_states = _fused_add(attn_out, hidden_states, post.weight, gate_up_w, post.variance_epsilon)
     gate, up = torch.split(gate_up, [self._fused_intermediate, self._fused_intermediate], dim=-1)
-    return hidden_states + self.mlp.down_proj(self.mlp.act_fn(gate) * up)
+    mlp_out = self.mlp.down_proj(self.mlp.act_fn(gate) * up)
+    if carry is not None and not self._fused_last:
+        carry["stream"] = hidden_states  # added by the next layer's fused input call
+        return mlp_out
+    return hidden_states + mlp_out
 
 
-def apply_fused_patch(model: LlamaForCausalLM, *, mlp: bool = False) -> LlamaForCausalLM:
+def apply_fused_patch(model: LlamaForCausalLM, *, mlp: bool = False, cross_layer: bool = False) -> LlamaForCausalLM:
     """Patch every decoder layer of ``model`` (idempotent).  ``mlp=True`` also fuses the
-    post-attention residual add + norm + gate/up projections."""
-    for layer in model.model.layers:
+    post-attention residual add + norm + gate/up projections; ``cross_layer=True`` (which
+    implies ``mlp``) also fuses each layer's MLP residual add into the next layer's input
+    norm + Q/K/V projection."""
+    mlp = mlp or cross_layer
+    layers = model.model.layers
+    n_run = min(len(layers), getattr(model.config, "num_hidden_layers", len(layers)))
+    carry = {} if cross_layer else None
+    for idx, layer in enumerate(layers):
         if hasattr(layer, _ORIGINAL):
             continue
         layer._fused_packed_qkv = pack_qkv_weight(layer.self_attn)
@@ -153,6 +185,10 @@ def apply_fused_patch(model: LlamaForCausalLM, *, mlp: bool = False) -> LlamaFor
         if mlp:
             layer._fused_packed_gate_up = pack_gate_up_weight(layer.mlp)
             layer._fused_intermediate = layer.mlp.gate_proj.weight.shape[0]
+        if carry is not None:
+            layer._fused_carry = carry  # shared by the layers of this model
+            layer._fused_first = idx == 0
+            layer._fused_last = idx == n_run - 1
         setattr(layer, _ORIGINAL, layer.forward)
         layer.forward = _patched_forward.__get__(layer, type(layer))
     return model
@@ -172,9 +208,9 @@ def remove_fused_patch(model: LlamaForCausalLM) -> LlamaForCausalLM:
 
 
 @contextmanager
-def fused_patch(model: LlamaForCausalLM, *, mlp: bool = False):
+def fused_patch(model: LlamaForCausalLM, *, mlp: bool = False, cross_layer: bool = False):
     """Apply the patch for the duration of a ``with`` block."""
-    apply_fused_patch(model, mlp=mlp)
+    apply_fused_patch(model, mlp=mlp, cross_layer=cross_layer)
     try:
         yield model
     finally:

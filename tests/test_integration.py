@@ -74,22 +74,36 @@ def test_mlp_patch_bookkeeping():
     remove_fused_patch(model)
 
 
+def test_cross_layer_patch_bookkeeping():
+    model = tiny_llama(layers=3)
+    with fused_patch(model, cross_layer=True):
+        layers = model.model.layers
+        assert all(hasattr(layer, "_fused_packed_gate_up") for layer in layers)  # implies mlp
+        assert layers[0]._fused_carry is layers[2]._fused_carry
+        assert [layer._fused_first for layer in layers] == [True, False, False]
+        assert [layer._fused_last for layer in layers] == [False, False, True]
+    assert not any(hasattr(layer, "_fused_carry") for layer in model.model.layers)
+
+
 def test_llama3_8b_config_shape():
     assert LLAMA3_8B_CONFIG["hidden_size"] + 2 * LLAMA3_8B_CONFIG["num_key_value_heads"] * \
         LLAMA3_8B_CONFIG["head_dim"] == 6144
 
 
+MODES = {"qkv": {}, "qkv+mlp": {"mlp": True}, "cross-layer": {"cross_layer": True}}
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("mlp", [False, True], ids=["qkv", "qkv+mlp"])
+@pytest.mark.parametrize("mode", list(MODES))
 @pytest.mark.parametrize("fixed", [False, True], ids=["auto", "fixed"])
-def test_patched_tiny_llama_matches_unpatched(fixed, mlp, monkeypatch):
+def test_patched_tiny_llama_matches_unpatched(fixed, mode, monkeypatch):
     if fixed:
         monkeypatch.setenv("TRITON_FUSED_DISABLE_AUTOTUNE", "1")
     model = tiny_llama("cuda", torch.bfloat16)
     ids = torch.randint(0, 500, (2, 24), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
     with torch.no_grad():
         ref = model(ids).logits.float()
-        with fused_patch(model, mlp=mlp):
+        with fused_patch(model, **MODES[mode]):
             got = model(ids).logits.float()
     rel = (got - ref).norm() / ref.norm()
     assert rel < 2e-2, float(rel)
@@ -108,12 +122,13 @@ def _prefill_then_decode(model, ids, cont):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mlp", [False, True], ids=["qkv", "qkv+mlp"])
-def test_patched_llama3_8b_two_layers_decode_and_prefill(mlp):
+@pytest.mark.parametrize("mode", list(MODES))
+def test_patched_llama3_8b_two_layers_decode_and_prefill(mode):
     """The Llama-3-8B layer shape (2 layers): prefill of 32 tokens (M = 32), then 4 decode
     steps (M = 1) through the KV cache, patched vs unpatched on the same token sequence.
-    With ``mlp`` the post-attention add + norm + gate/up (N = 2 x 14336) runs through the
-    fused op too.  (Greedy generation is not compared: with random weights the logits are
+    With "qkv+mlp" the post-attention add + norm + gate/up (N = 2 x 14336) runs through the
+    fused op too; with "cross-layer" the second layer's input call also takes the first
+    layer's MLP output and residual stream (R = 1).  (Greedy generation is not compared: with random weights the logits are
     nearly flat, and a rounding-level difference can change the argmax and so every later
     step's input.)"""
     model = build_llama3_8b(dtype=torch.bfloat16, device="cuda", num_hidden_layers=2)
@@ -122,7 +137,7 @@ def test_patched_llama3_8b_two_layers_decode_and_prefill(mlp):
     cont = torch.randint(0, 128256, (1, 4), device="cuda", generator=gen)
     with torch.no_grad():
         ref = _prefill_then_decode(model, ids, cont)
-        with fused_patch(model, mlp=mlp):
+        with fused_patch(model, **MODES[mode]):
             got = _prefill_then_decode(model, ids, cont)
     for a, b in zip(got, ref):
         rel = (a - b).norm() / b.norm()
