@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nkb = kb1 - kb0;
   const int n_base = blockIdx.y * NT * kTileRows;
   constexpr uint32_t kTmemCols = tmem_cols_for(NT * MPAD);
+  constexpr int kBoxTiles = decode_box_tiles(NT);
 
   // ---------------------------------------------------------------- setup
   if (threadIdx.x == 0) {
@@ -152,7 +153,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i == pre) ok = mbar_wait(acts_bar, 0);
         if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
         mbar_arrive_expect_tx(&full[s], tx);
-        tma_load_2d_hint(ring + s * L.stage_bytes, &tmW, &full[s], (kb0 + i) * kKBlock, n_base, pol_w);
+        // A stage holds NT 128-row tiles: one box of NT x 128 rows for NT <= 2, else NT
+        // boxes of 128 rows (a TMA box dimension is at most 256).
+#pragma unroll
+        for (int j = 0; j < NT; j += kBoxTiles)
+          tma_load_2d_hint(ring + s * L.stage_bytes + j * kWTileBytes, &tmW, &full[s], (kb0 + i) * kKBlock,
+                           n_base + j * kTileRows, pol_w);
         ++issued;
         if (++s == stages) {
           s = 0;
@@ -474,17 +480,21 @@ auto kernel_ptr(bool bf16) {
 
 using KernelFn = void (*)(CUtensorMap, DecodeParams, int);
 
+// Tile rows per CTA: 1 or 2 for every MPAD; 3 to 5 (wide weights: more SMs in one wave)
+// for MPAD 16 and 32.
+constexpr int kMaxNT = 5;
+
 KernelFn pick_kernel(int mpad, int nt, bool bf16) {
-  if (nt == 1) {
-    if (mpad == 16) return kernel_ptr<16, 1>(bf16);
-    if (mpad == 32) return kernel_ptr<32, 1>(bf16);
-    if (mpad == 64) return kernel_ptr<64, 1>(bf16);
-  } else {
-    if (mpad == 16) return kernel_ptr<16, 2>(bf16);
-    if (mpad == 32) return kernel_ptr<32, 2>(bf16);
-    if (mpad == 64) return kernel_ptr<64, 2>(bf16);
+  switch (nt) {
+    case 1: return mpad == 16 ? kernel_ptr<16, 1>(bf16) : mpad == 32 ? kernel_ptr<32, 1>(bf16)
+                 : mpad == 64 ? kernel_ptr<64, 1>(bf16) : nullptr;
+    case 2: return mpad == 16 ? kernel_ptr<16, 2>(bf16) : mpad == 32 ? kernel_ptr<32, 2>(bf16)
+                 : mpad == 64 ? kernel_ptr<64, 2>(bf16) : nullptr;
+    case 3: return mpad == 16 ? kernel_ptr<16, 3>(bf16) : mpad == 32 ? kernel_ptr<32, 3>(bf16) : nullptr;
+    case 4: return mpad == 16 ? kernel_ptr<16, 4>(bf16) : mpad == 32 ? kernel_ptr<32, 4>(bf16) : nullptr;
+    case 5: return mpad == 16 ? kernel_ptr<16, 5>(bf16) : mpad == 32 ? kernel_ptr<32, 5>(bf16) : nullptr;
+    default: return nullptr;
   }
-  return nullptr;
 }
 
 cudaLaunchConfig_t base_config(const DecodeConfig& c, int tiles, cudaLaunchAttribute* attr, int* na) {
@@ -571,8 +581,9 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
   DecodeConfig best{};
   const int KB = (H + kKBlock - 1) / kKBlock;
   long best_score = -1;
-  for (int nt = 1; nt <= 2; ++nt) {
+  for (int nt = 1; nt <= kMaxNT; ++nt) {
     if (force_nt && nt != force_nt) continue;
+    if (!pick_kernel(mpad, nt, true)) continue;
     const int tiles = (N + nt * kTileRows - 1) / (nt * kTileRows);
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;

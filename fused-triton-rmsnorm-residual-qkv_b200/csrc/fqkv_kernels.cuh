@@ -312,6 +312,9 @@ struct DecodeConfig {
 };
 
 int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg);
+// 128-row weight tiles per TMA box of the decode kernel's weight map: one box per stage
+// for NT <= 2, else NT boxes of 128 rows (a box dimension is at most 256 elements).
+__host__ __device__ constexpr int decode_box_tiles(int nt) { return nt <= 2 ? nt : 1; }
 size_t decode_smem_bytes(const DecodeConfig& c, int kb_total);
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream);

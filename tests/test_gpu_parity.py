@@ -100,6 +100,16 @@ def test_post_attention_gate_up_shape(M):
     run_case(M, 4096, 2 * 14336, torch.bfloat16, seed=500 + M)
 
 
+@pytest.mark.parametrize("N", [22528, 25600, 28672])
+@pytest.mark.parametrize("M", [1, 16, 32])
+def test_wide_weight_decode(M, N):
+    """Weights of 176 / 200 / 224 row tiles: for one co-resident wave on more SMs the decode
+    kernel takes 4 / 3 / 5 tiles of 128 rows per CTA (NT > 2: one TMA box per tile)."""
+    info = _lib.query_schedule(M, 4096, N, _lib.BF16)
+    print(f"M={M} N={N}: {info}")
+    run_case(M, 4096, N, torch.bfloat16, seed=N + M)
+
+
 def test_cpu_ref_shape_on_gpu():
     """configs[0]'s shape (4 tokens, H=256, N=512) in bf16 (the kernels take 16-bit data)."""
     run_case(4, 256, 512, torch.bfloat16, seed=1)
