@@ -446,11 +446,22 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
 
         import torch.distributed as dist
 
-        # Rank 0 prints exactly one JSON line on stdout: NCCL's own messages (e.g. its
-        # version banner) go to stderr unless the caller chose a destination.
+        # Rank 0 prints exactly one JSON line on stdout.  NCCL's own messages go to stderr
+        # unless the caller chose a destination, and its version banner, which it writes to
+        # the process's standard output when the communicator comes up, is kept off stdout
+        # by pointing file descriptor 1 at stderr until the first collective has run.
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
         pg = dist
 
     def barrier():
