@@ -24,7 +24,7 @@ residual add with the updated residual returned).  32 distinct seeded weight set
              M=512/2048/8192 (TFLOPS), the unfused PyTorch path (cuBLAS) on the same
              inputs as the GPU comparator, a streaming-read bandwidth for context, and
              a 4-layer Llama-3-8B stack (M=1/16) unpatched vs the integration patch's
-             three modes (Q/K/V, + MLP gate/up, cross-layer).
+             modes (Q/K/V, + MLP gate/up, cross-layer, + one-launch Q/K/V rotary split).
 With N > 1 (torchrun) the layer is head-sharded column-parallel: each rank owns N/P
 weight rows and computes them with replicated inputs; no collective runs inside the
 timed region.  After timing, an NCCL all-gather reassembles one step for a check
@@ -402,15 +402,17 @@ def run_layer_stack(dev, n_layers: int = 4, ms=(1, 16), steps: int = 50) -> dict
     """Model-level check of the integration: a stack of Llama-3-8B decoder layers (random
     init, bf16, no KV cache, causal attention over the M tokens) and the final norm,
     graph-timed per forward of M tokens.  Unpatched PyTorch against the patch in its three
-    modes: Q/K/V only (the reference's patch), + post-attention add/norm/gate-up, and
-    cross-layer (each layer's MLP residual add fused into the next layer's input call)."""
+    modes: Q/K/V only (the reference's patch), + post-attention add/norm/gate-up,
+    cross-layer (each layer's MLP residual add fused into the next layer's input call), and
+    cross-layer with the Q/K/V split + rotary embedding in one launch."""
     from contextlib import nullcontext
 
     from integration import build_llama3_8b, fused_patch
 
     model = build_llama3_8b(dtype=torch.bfloat16, device=str(dev), num_hidden_layers=n_layers)
     inner = model.model
-    modes = (("unpatched", None), ("qkv", {}), ("qkv+mlp", {"mlp": True}), ("cross-layer", {"cross_layer": True}))
+    modes = (("unpatched", None), ("qkv", {}), ("qkv+mlp", {"mlp": True}), ("cross-layer", {"cross_layer": True}),
+             ("cross-layer+rope", {"cross_layer": True, "rope": True}))
     out = {"layers": n_layers, "steps": steps, "unit": "us per forward of M tokens through all layers"}
     with torch.no_grad():
         for M in ms:

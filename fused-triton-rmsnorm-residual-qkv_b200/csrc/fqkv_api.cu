@@ -277,7 +277,52 @@ cudaError_t ensure_smem_attr(const void* func, size_t bytes) {
 
 using namespace fqkv;
 
-extern "C" FQKV_API int fqkv_version(void) { return 100; }
+extern "C" FQKV_API int fqkv_version(void) { return 101; }
+
+// The projection's [M, (n_q + 2 n_kv) d] output to head-major Q, K, V with the rotary
+// embedding on Q and K (fqkv_rope.cu): what llama3_patch.py:156-168 does in PyTorch after
+// the fused call (split, view as heads, transpose, apply_rotary_pos_emb).
+extern "C" FQKV_API int fqkv_rope_split(const void* qkv, int64_t ldq, const void* cos, const void* sin,
+                                        int64_t cos_batch, void* q, void* k, void* v, int64_t B, int64_t S,
+                                        int n_q_heads, int n_kv_heads, int head_dim, int dtype, void* stream) {
+  if (dtype != FQKV_F16 && dtype != FQKV_BF16)
+    return fail(FQKV_ERR_DTYPE, "dtype %d is not supported (fp16 = 0, bf16 = 1)", dtype);
+  if (!qkv || !cos || !sin || !q || !k || !v) return fail(FQKV_ERR_NULL, "qkv, cos, sin, q, k and v must be non-null");
+  if (B <= 0 || S <= 0 || n_q_heads <= 0 || n_kv_heads <= 0)
+    return fail(FQKV_ERR_SHAPE, "B, S and the head counts must be positive");
+  if (head_dim <= 0 || head_dim % 16)
+    return fail(FQKV_ERR_SHAPE, "head_dim %d must be a positive multiple of 16", head_dim);
+  const int64_t width = (int64_t)(n_q_heads + 2 * n_kv_heads) * head_dim;
+  if (ldq < width) return fail(FQKV_ERR_SHAPE, "ldq %lld is smaller than the row (%lld)", (long long)ldq, (long long)width);
+  if (cos_batch != 1 && cos_batch != B)
+    return fail(FQKV_ERR_SHAPE, "cos / sin must hold 1 or B = %lld batch rows (got %lld)", (long long)B,
+                (long long)cos_batch);
+  if (!aligned16(qkv) || !aligned16(cos) || !aligned16(sin) || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
+      ldq % 8)
+    return fail(FQKV_ERR_ALIGN, "every pointer must be 16-byte aligned and ldq a multiple of 8");
+  const int64_t M = B * S;
+  const int64_t qkv_b = mat_bytes(M, width, ldq), cs_b = cos_batch * S * head_dim * 2;
+  const int64_t q_b = M * n_q_heads * head_dim * 2, kv_b = M * n_kv_heads * head_dim * 2;
+  const void* ins[3] = {qkv, cos, sin};
+  const int64_t in_b[3] = {qkv_b, cs_b, cs_b};
+  void* outs[3] = {q, k, v};
+  const int64_t out_b[3] = {q_b, kv_b, kv_b};
+  for (int i = 0; i < 3; ++i) {
+    for (int j = 0; j < 3; ++j)
+      if (overlaps(outs[i], out_b[i], ins[j], in_b[j]))
+        return fail(FQKV_ERR_ALIAS, "q, k and v must not overlap qkv, cos or sin");
+    for (int j = i + 1; j < 3; ++j)
+      if (overlaps(outs[i], out_b[i], outs[j], out_b[j])) return fail(FQKV_ERR_ALIAS, "q, k and v must not overlap");
+  }
+  DeviceInfo d;
+  if (int rc = device_info(&d)) return rc;
+  if (d.major != 10) return fail(FQKV_ERR_DEVICE, "compute capability %d.%d is not sm_100", d.major, d.minor);
+  RopeParams rp{static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(cos), static_cast<const uint16_t*>(sin),
+                static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), static_cast<uint16_t*>(v), M, S, ldq,
+                cos_batch == 1 ? 0 : S * head_dim, n_q_heads, n_kv_heads, head_dim};
+  const cudaError_t e = launch_rope_split(rp, dtype == FQKV_BF16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? 0 : cuda_fail(e, "rope split kernel launch");
+}
 
 extern "C" FQKV_API const char* fqkv_last_error(void) { return t_last_error.c_str(); }
 

@@ -9,6 +9,20 @@
 namespace fqkv {
 
 // ------------------------------------------------------------------ parameters
+// Packed projection output -> head-major Q, K, V with the rotary embedding on Q and K
+// (fqkv_rope.cu).  Rows m = b * S + s of qkv hold [Q heads | K heads | V heads].
+struct RopeParams {
+  const uint16_t* qkv;        // [M, (n_q + 2 n_kv) * head_dim], row stride ldq
+  const uint16_t* cos;        // [B or 1, S, head_dim]
+  const uint16_t* sin;        // same layout as cos
+  uint16_t* q;                // [B, n_q, S, head_dim]
+  uint16_t* k;                // [B, n_kv, S, head_dim]
+  uint16_t* v;                // [B, n_kv, S, head_dim]
+  int64_t M, S, ldq;
+  int64_t cs_batch_stride;    // S * head_dim, or 0 when cos / sin are shared by the batch
+  int n_q, n_kv, head_dim;
+};
+
 struct PrepassParams {
   const uint16_t* x;
   const uint16_t* r;  // nullable
@@ -343,6 +357,7 @@ struct GemmConfig {
   int pair;     // 1: 2-CTA clusters computing 256-row tiles (tcgen05 cta_group::2)
 };
 int gemm_pick_config(int M, int H, int N, int sm_count, GemmConfig* cfg);
+cudaError_t launch_rope_split(const RopeParams& p, bool bf16, cudaStream_t stream);
 cudaError_t launch_gemm(const GemmConfig& c, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
                         const GemmParams& p, bool bf16, bool pdl, cudaStream_t stream);
 

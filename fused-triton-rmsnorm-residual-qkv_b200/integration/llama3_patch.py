@@ -29,6 +29,10 @@ launch adds the two (bit-exact), normalises and projects.  The last layer return
 full stream, so the final norm is unchanged.  With it, hidden states collected between
 layers (``output_hidden_states``) are the MLP outputs, not the stream.
 
+``rope=True`` replaces the split / view / transpose / ``apply_rotary_pos_emb`` sequence after
+the fused Q/K/V call by ``qkv_rope_split``: one launch that writes head-major Q, K, V with
+Q and K rotated, bit-identical to that sequence.
+
 Written against transformers 5.5 (``LlamaDecoderLayer.forward`` / ``LlamaAttention``).
 """
 from __future__ import annotations
@@ -50,6 +54,7 @@ from triton_fused_rmsnorm_qkv import (
     fused_add_rmsnorm_matmul,
     fused_rmsnorm_residual_matmul,
     fused_rmsnorm_residual_matmul_fixed,
+    qkv_rope_split,
 )
 
 LLAMA3_8B_CONFIG = dict(
@@ -70,7 +75,7 @@ LLAMA3_8B_CONFIG = dict(
 
 _ORIGINAL = "_fused_original_forward"
 _LAYER_ATTRS = ("_fused_packed_qkv", "_fused_H_kv", "_fused_packed_gate_up", "_fused_intermediate",
-                "_fused_carry", "_fused_first", "_fused_last")
+                "_fused_carry", "_fused_first", "_fused_last", "_fused_rope")
 
 
 def _fixed() -> bool:
@@ -143,12 +148,15 @@ def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None
         # The previous layer's MLP output arrives with the stream it belongs to.
         qkv, hidden_states = _fused_add(hidden_states, pending, self.input_layernorm.weight, self._fused_packed_qkv,
                                         self.input_layernorm.variance_epsilon)
-    q, k, v = torch.split(qkv, [h_q, h_kv, h_kv], dim=-1)
-    q = q.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
-    k = k.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
-    v = v.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
     cos, sin = position_embeddings
-    q, k = apply_rotary_pos_emb(q, k, cos, sin)
+    if getattr(self, "_fused_rope", False):
+        q, k, v = qkv_rope_split(qkv, cos, sin, h_q // attn.head_dim, h_kv // attn.head_dim, attn.head_dim)
+    else:
+        q, k, v = torch.split(qkv, [h_q, h_kv, h_kv], dim=-1)
+        q = q.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
+        k = k.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
+        v = v.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
+        q, k = apply_rotary_pos_emb(q, k, cos, sin)
     if past_key_values is not None:
         k, v = past_key_values.update(k, v, attn.layer_idx)
     attend = ALL_ATTENTION_FUNCTIONS.get_interface(attn.config._attn_implementation, eager_attention_forward)
@@ -168,11 +176,13 @@ def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None
     return hidden_states + mlp_out
 
 
-def apply_fused_patch(model: LlamaForCausalLM, *, mlp: bool = False, cross_layer: bool = False) -> LlamaForCausalLM:
+def apply_fused_patch(model: LlamaForCausalLM, *, mlp: bool = False, cross_layer: bool = False,
+                      rope: bool = False) -> LlamaForCausalLM:
     """Patch every decoder layer of ``model`` (idempotent).  ``mlp=True`` also fuses the
     post-attention residual add + norm + gate/up projections; ``cross_layer=True`` (which
     implies ``mlp``) also fuses each layer's MLP residual add into the next layer's input
-    norm + Q/K/V projection."""
+    norm + Q/K/V projection; ``rope=True`` splits Q/K/V head-major and rotates Q and K in
+    one launch."""
     mlp = mlp or cross_layer
     layers = model.model.layers
     n_run = min(len(layers), getattr(model.config, "num_hidden_layers", len(layers)))
@@ -185,6 +195,8 @@ def apply_fused_patch(model: LlamaForCausalLM, *, mlp: bool = False, cross_layer
         if mlp:
             layer._fused_packed_gate_up = pack_gate_up_weight(layer.mlp)
             layer._fused_intermediate = layer.mlp.gate_proj.weight.shape[0]
+        if rope:
+            layer._fused_rope = True
         if carry is not None:
             layer._fused_carry = carry  # shared by the layers of this model
             layer._fused_first = idx == 0
@@ -208,9 +220,9 @@ def remove_fused_patch(model: LlamaForCausalLM) -> LlamaForCausalLM:
 
 
 @contextmanager
-def fused_patch(model: LlamaForCausalLM, *, mlp: bool = False, cross_layer: bool = False):
+def fused_patch(model: LlamaForCausalLM, *, mlp: bool = False, cross_layer: bool = False, rope: bool = False):
     """Apply the patch for the duration of a ``with`` block."""
-    apply_fused_patch(model, mlp=mlp, cross_layer=cross_layer)
+    apply_fused_patch(model, mlp=mlp, cross_layer=cross_layer, rope=rope)
     try:
         yield model
     finally:

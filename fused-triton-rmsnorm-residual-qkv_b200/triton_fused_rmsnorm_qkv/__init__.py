@@ -2,7 +2,8 @@
 
 Import-compatible with the reference package ``triton_fused_rmsnorm_qkv``
 (``src/triton_fused_rmsnorm_qkv/__init__.py:1-17``): the same six names, plus
-``fused_add_rmsnorm_matmul`` (returns the updated residual as well).  The GPU entry
+``fused_add_rmsnorm_matmul`` (returns the updated residual as well) and
+``qkv_rope_split`` (head-major Q/K/V with the rotary embedding, one launch).  The GPU entry
 points run sm_100a CUDA kernels from ``libfqkv.so``; they raise if that library is
 missing instead of falling back to anything else.
 """
@@ -15,6 +16,7 @@ from .kernel import (
     fused_rmsnorm_residual_qkv,
     fused_rmsnorm_residual_qkv_fixed,
     get_autotune_best_config,
+    qkv_rope_split,
 )
 
 __all__ = [
@@ -26,4 +28,5 @@ __all__ = [
     "get_autotune_best_config",
     "fused_add_rmsnorm_matmul",
     "device_status",
+    "qkv_rope_split",
 ]

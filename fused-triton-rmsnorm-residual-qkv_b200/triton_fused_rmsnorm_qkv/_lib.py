@@ -32,6 +32,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libfqkv.so"
 EXPORTED_SYMBOLS = (
     "fqkv_launch",
     "fqkv_launch_noalloc",
+    "fqkv_rope_split",
     "fqkv_workspace_bytes",
     "fqkv_query_schedule",
     "fqkv_last_error",
@@ -79,6 +80,8 @@ def load() -> ctypes.CDLL:
     lib.fqkv_device_status.restype = i32
     lib.fqkv_version.argtypes = []
     lib.fqkv_version.restype = i32
+    lib.fqkv_rope_split.argtypes = [vp, i64, vp, vp, i64, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp]
+    lib.fqkv_rope_split.restype = i32
     _lib = lib
     return lib
 
@@ -103,6 +106,12 @@ def launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx,
            dtype, schedule, flags, ws_ptr, ws_bytes, stream) -> int:
     return load().fqkv_launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw,
                               ldo, ldro, ctypes.c_float(eps), dtype, schedule, flags, ws_ptr, ws_bytes, stream)
+
+
+def rope_split(qkv_ptr, ldq, cos_ptr, sin_ptr, cos_batch, q_ptr, k_ptr, v_ptr, B, S, n_q, n_kv, head_dim,
+               dtype, stream) -> int:
+    return load().fqkv_rope_split(qkv_ptr, ldq, cos_ptr, sin_ptr, cos_batch, q_ptr, k_ptr, v_ptr, B, S, n_q, n_kv,
+                                  head_dim, dtype, stream)
 
 
 def workspace_bytes(M: int, H: int, N: int, dtype: int, schedule: int) -> int:

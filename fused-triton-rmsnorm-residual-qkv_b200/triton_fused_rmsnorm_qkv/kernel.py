@@ -239,6 +239,59 @@ def fused_rmsnorm_residual_qkv(
     return q, k, v
 
 
+def qkv_rope_split(
+    qkv: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    n_q_heads: int,
+    n_kv_heads: int,
+    head_dim: Optional[int] = None,
+):
+    """Split a packed projection output into head-major Q, K, V and rotate Q and K.
+
+    ``qkv`` is (B, S, (n_q + 2 n_kv) * d), the output of the fused call on the packed
+    ``[Wq; Wk; Wv]`` weight.  Returns ``q`` (B, n_q, S, d), ``k`` and ``v`` (B, n_kv, S, d),
+    contiguous, with ``x * cos + rotate_half(x) * sin`` applied to q and k: one CUDA launch
+    for what the Llama integration does with split / view / transpose and transformers'
+    ``apply_rotary_pos_emb`` (llama3_patch.py:156-168), and bit-identical to it.  ``cos`` and
+    ``sin`` are (B, S, d), (1, S, d) or (S, d) in qkv's dtype, as the model's rotary
+    embedding returns them.
+    """
+    if qkv.dim() != 3:
+        raise ValueError(f"qkv must be (B, S, width), got shape {tuple(qkv.shape)}")
+    if qkv.dtype not in _DTYPE_CODE:
+        raise TypeError(f"qkv must be float16 or bfloat16, got {qkv.dtype}")
+    B, S, W = qkv.shape
+    heads = n_q_heads + 2 * n_kv_heads
+    if head_dim is None:
+        head_dim = W // heads
+    if heads * head_dim != W:
+        raise ValueError(f"qkv width {W} is not ({n_q_heads} + 2 * {n_kv_heads}) * {head_dim}")
+    tabs = []
+    for name, t in (("cos", cos), ("sin", sin)):
+        if t.dtype != qkv.dtype or t.device != qkv.device:
+            raise TypeError(f"{name} must have qkv's dtype and device ({qkv.dtype}, {qkv.device})")
+        if t.dim() == 2:
+            t = t.unsqueeze(0)
+        if t.dim() != 3 or t.shape[1:] != (S, head_dim) or t.shape[0] not in (1, B):
+            raise ValueError(f"{name} must be (B, S, d), (1, S, d) or (S, d); got {tuple(t.shape)}")
+        tabs.append(t.contiguous())
+    if tabs[0].shape[0] != tabs[1].shape[0]:
+        raise ValueError("cos and sin must have the same batch size")
+    rows = _rows(qkv, B * S, W)
+    q = torch.empty(B, n_q_heads, S, head_dim, dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty(B, n_kv_heads, S, head_dim, dtype=qkv.dtype, device=qkv.device)
+    v = torch.empty_like(k)
+    dev = qkv.device
+    ctx = contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
+    with ctx:
+        rc = _lib.rope_split(rows.data_ptr(), _row_stride(rows), tabs[0].data_ptr(), tabs[1].data_ptr(),
+                             tabs[0].shape[0], q.data_ptr(), k.data_ptr(), v.data_ptr(), B, S, n_q_heads, n_kv_heads,
+                             head_dim, _DTYPE_CODE[qkv.dtype], _current_stream(dev.index))
+    _lib.check(rc, "fqkv_rope_split")
+    return q, k, v
+
+
 def fused_rmsnorm_residual_matmul_fixed(
     x: torch.Tensor,
     residual: Optional[torch.Tensor],

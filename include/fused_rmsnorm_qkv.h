@@ -152,6 +152,26 @@ FQKV_API int fqkv_launch_noalloc(const void* x, const void* residual, const void
                 int64_t ldx, int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro,
                 float eps, int dtype, int flags, void* stream);
 
+/*
+ * Split the projection's output into head-major Q, K, V and rotate Q and K (rotary
+ * position embedding), in one launch.  Replaces what the Llama integration does after
+ * the fused call (llama3_patch.py:156-168): split by [n_q d, n_kv d, n_kv d], view as
+ * heads, transpose to (B, heads, S, d) and apply transformers' apply_rotary_pos_emb,
+ *   x_rot = x * cos + rotate_half(x) * sin,  rotate_half(x) = cat(-x[d/2:], x[:d/2]).
+ * Each product is rounded to the dtype and their sum formed in fp32 and rounded, as
+ * PyTorch's 16-bit elementwise ops do, so the result is bit-identical to that sequence.
+ *   qkv   [B * S, (n_q + 2 n_kv) * d]  dtype, row stride ldq (rows m = b * S + s)
+ *   cos   [cos_batch, S, d]  dtype, contiguous; cos_batch is 1 (shared) or B
+ *   sin   same layout as cos
+ *   q     [B, n_q, S, d]   k, v  [B, n_kv, S, d]   dtype, contiguous, not overlapping
+ *         each other or the inputs
+ * d must be a multiple of 16, every pointer 16-byte aligned and ldq a multiple of 8.
+ * No counterpart in the reference's C surface (its integration does this in PyTorch).
+ */
+FQKV_API int fqkv_rope_split(const void* qkv, int64_t ldq, const void* cos, const void* sin,
+                int64_t cos_batch, void* q, void* k, void* v, int64_t B, int64_t S,
+                int n_q_heads, int n_kv_heads, int head_dim, int dtype, void* stream);
+
 /* ABI version (major * 100 + minor). */
 FQKV_API int fqkv_version(void);
 

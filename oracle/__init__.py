@@ -16,3 +16,4 @@ from .rmsnorm_qkv import (  # noqa: F401
     ulp,
     within_bars,
 )
+from .rope import make_rope_case, rope_split  # noqa: F401,E402

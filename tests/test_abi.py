@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert _lib.version() == 100
+    assert _lib.version() == 101
 
 
 FAKE = 0x100000  # 16-byte aligned, never dereferenced: validation fails before any launch
@@ -121,3 +121,31 @@ def test_workspace_size_rejects_bad_arguments():
         _lib.workspace_bytes(0, 4096, 6144, _lib.BF16, -1)
     with pytest.raises(TypeError):
         _lib.workspace_bytes(4, 4096, 6144, 9, -1)
+
+
+def rope_call(**kw):
+    a = dict(qkv=1 << 32, ldq=6144, cos=2 << 32, sin=3 << 32, cb=1, q=4 << 32, k=5 << 32, v=6 << 32, B=2, S=3,
+             nq=32, nkv=8, d=128, dtype=_lib.BF16, stream=None)
+    a.update(kw)
+    return _lib.rope_split(a["qkv"], a["ldq"], a["cos"], a["sin"], a["cb"], a["q"], a["k"], a["v"], a["B"], a["S"],
+                           a["nq"], a["nkv"], a["d"], a["dtype"], a["stream"])
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(qkv=None), _lib.ERR_NULL),
+    (dict(sin=None), _lib.ERR_NULL),
+    (dict(v=None), _lib.ERR_NULL),
+    (dict(dtype=_lib.F32), _lib.ERR_DTYPE),
+    (dict(B=0), _lib.ERR_SHAPE),
+    (dict(nkv=0), _lib.ERR_SHAPE),
+    (dict(d=120), _lib.ERR_SHAPE),           # head_dim must be a multiple of 16
+    (dict(ldq=6143), _lib.ERR_SHAPE),        # row shorter than (n_q + 2 n_kv) d
+    (dict(cb=3), _lib.ERR_SHAPE),            # cos / sin hold 1 or B batch rows
+    (dict(ldq=6148), _lib.ERR_ALIGN),        # row stride not a multiple of 8 elements
+    (dict(q=(4 << 32) + 8), _lib.ERR_ALIGN),
+    (dict(q=(1 << 32) + 64), _lib.ERR_ALIAS),  # q inside qkv
+    (dict(k=(4 << 32) + 4096), _lib.ERR_ALIAS),  # k inside q
+])
+def test_rope_split_rejects_before_any_cuda_call(kw, code):
+    """fqkv_rope_split validates its arguments before touching the device."""
+    assert rope_call(**kw) == code, _lib.last_error()

@@ -90,7 +90,8 @@ def test_llama3_8b_config_shape():
         LLAMA3_8B_CONFIG["head_dim"] == 6144
 
 
-MODES = {"qkv": {}, "qkv+mlp": {"mlp": True}, "cross-layer": {"cross_layer": True}}
+MODES = {"qkv": {}, "qkv+mlp": {"mlp": True}, "cross-layer": {"cross_layer": True},
+         "all": {"cross_layer": True, "rope": True}}
 
 
 @pytest.mark.gpu

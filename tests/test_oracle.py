@@ -79,3 +79,22 @@ def test_parity_metrics():
     a = torch.tensor([1.0, 2.0, 3.0])
     m = parity_metrics(a + torch.tensor([0.0, 0.01, 0.0]), a)
     assert abs(m["max_abs"] - 0.01) < 1e-6 and m["nonfinite"] == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("B,S,n_q,n_kv,d,cb", [(1, 1, 32, 8, 128, 1), (2, 7, 4, 2, 64, 2), (3, 5, 8, 8, 128, 1)])
+def test_rope_oracle_matches_transformers(B, S, n_q, n_kv, d, cb, dtype):
+    """The Q/K/V split + rotary oracle is bit-identical to transformers' own
+    apply_rotary_pos_emb on the same split (llama3_patch.py:156-168)."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+
+    from oracle import make_rope_case, rope_split
+
+    qkv, cos, sin = make_rope_case(B, S, n_q, n_kv, d, dtype, seed=B * 100 + S, cos_batch=cb)
+    q, k, v = rope_split(qkv, cos, sin, n_q, n_kv, d)
+    qs, ks, vs = torch.split(qkv, [n_q * d, n_kv * d, n_kv * d], dim=-1)
+    qh = qs.reshape(B, S, n_q, d).transpose(1, 2)
+    kh = ks.reshape(B, S, n_kv, d).transpose(1, 2)
+    qr, kr = apply_rotary_pos_emb(qh, kh, cos.expand(B, S, d), sin.expand(B, S, d))
+    assert torch.equal(q, qr) and torch.equal(k, kr)
+    assert torch.equal(v, vs.reshape(B, S, n_kv, d).transpose(1, 2))
