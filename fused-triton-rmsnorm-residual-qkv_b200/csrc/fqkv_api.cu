@@ -89,19 +89,22 @@ int get_encode(EncodeTiledFn* fn) {
   return 0;
 }
 
-// 2-D K-major tensor map over a [rows, cols] matrix of 16-bit elements with row
-// stride ld (elements), 128-byte swizzle, box {64, box_rows}.
+// Element kinds of make_map: the dtype codes FQKV_F16 / FQKV_BF16, and e4m3 bytes.
+constexpr int kMapBF16 = FQKV_BF16, kMapE4M3 = 2;
+
+// 2-D K-major tensor map over a [rows, cols] matrix with row stride ld (elements), 128-byte
+// swizzle: 16-bit elements with box {64, box_rows}, or one-byte e4m3 elements with box
+// {128, box_rows} -- 128-byte box rows either way.
 // Encoded maps are cached by (address, shape, stride, box, dtype): a model calls the op
 // with the same weight (and often the same activation buffers) every step, and a map
 // holds only the address and the layout.
-using MapKey = std::tuple<const void*, int64_t, int64_t, int64_t, int, bool>;
+using MapKey = std::tuple<const void*, int64_t, int64_t, int64_t, int, int>;
 std::mutex g_map_mu;
 std::map<MapKey, CUtensorMap> g_map_cache;
 constexpr size_t kMapCacheMax = 1024;
 
-int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
-             bool bf16) {
-  const MapKey key{base, rows, cols, ld, box_rows, bf16};
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, int kind) {
+  const MapKey key{base, rows, cols, ld, box_rows, kind};
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
     auto it = g_map_cache.find(key);
@@ -113,11 +116,14 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
   EncodeTiledFn enc;
   if (int rc = get_encode(&enc)) return rc;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  const cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  const bool e4m3 = kind == kMapE4M3;
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * (e4m3 ? 1 : 2))};
+  const cuuint32_t box[2] = {e4m3 ? 128u : 64u, (cuuint32_t)box_rows};  // 128-byte box rows either way
   const cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUtensorMapDataType dt = e4m3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                      : kind == kMapBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -150,13 +156,14 @@ struct Problem {
   const void *x, *r, *g, *w;
   void *out, *rout;
   int dtype, gdt, schedule, flags;
+  bool w16 = true;  // w is a 16-bit weight; false: the caller checks its own weight layout
 };
 
 bool tma_eligible(const Problem& p) {
-  if (p.H % 8 || p.ldx % 8 || p.ldw % 8) return false;
+  if (p.H % 8 || p.ldx % 8 || (p.w16 && p.ldw % 8)) return false;
   if (p.r && p.ldr % 8) return false;
   if (p.rout && p.ldro % 8) return false;
-  if (!aligned16(p.x) || !aligned16(p.w) || !aligned16(p.g) || (p.r && !aligned16(p.r)) ||
+  if (!aligned16(p.x) || (p.w16 && !aligned16(p.w)) || !aligned16(p.g) || (p.r && !aligned16(p.r)) ||
       (p.rout && !aligned16(p.rout)))
     return false;
   if (p.H > kPrepassMaxH) return false;
@@ -207,7 +214,7 @@ int auto_schedule_for(int64_t M, int64_t H, int64_t N, const DeviceInfo* dev) {
 }
 
 int validate(const Problem& p) {
-  if (!p.x || !p.g || !p.w || !p.out)
+  if (!p.x || !p.g || (p.w16 && !p.w) || !p.out)
     return fail(FQKV_ERR_NULL, "x, rms_weight, weight and out must be non-null");
   if (p.dtype != FQKV_F16 && p.dtype != FQKV_BF16)
     return fail(FQKV_ERR_DTYPE, "dtype %d is not supported (fp16 = 0, bf16 = 1)", p.dtype);
@@ -225,7 +232,7 @@ int validate(const Problem& p) {
   if (p.flags & ~(FQKV_FLAG_PDL | FQKV_FLAG_STATIC_WEIGHTS))
     return fail(FQKV_ERR_SCHEDULE, "unknown flag bits 0x%x", p.flags);
   const int64_t xb = mat_bytes(p.M, p.H, p.ldx), ob = mat_bytes(p.M, p.N, p.ldo);
-  const int64_t wb = mat_bytes(p.N, p.H, p.ldw);
+  const int64_t wb = p.w16 ? mat_bytes(p.N, p.H, p.ldw) : 0;  // 0: overlaps() ignores it
   const int64_t rb = p.r ? mat_bytes(p.M, p.H, p.ldr) : 0, rob = p.rout ? mat_bytes(p.M, p.H, p.ldro) : 0;
   if (overlaps(p.out, ob, p.x, xb) || overlaps(p.out, ob, p.r, rb) || overlaps(p.out, ob, p.w, wb) ||
       overlaps(p.out, ob, p.rout, rob))
@@ -282,6 +289,51 @@ extern "C" FQKV_API int fqkv_version(void) { return 101; }
 // The projection's [M, (n_q + 2 n_kv) d] output to head-major Q, K, V with the rotary
 // embedding on Q and K (fqkv_rope.cu): what llama3_patch.py:156-168 does in PyTorch after
 // the fused call (split, view as heads, transpose, apply_rotary_pos_emb).
+// The op with e4m3 weights and an fp32 scale per weight row: the fused decode kernel
+// streams the one-byte weight and converts it exactly to the dtype in shared memory, and
+// the row scale multiplies the k-summed value once.  Decode schedule only (M <= 64 with a
+// fitting configuration).
+extern "C" FQKV_API int fqkv_launch_fp8w(const void* x, const void* residual, const void* rms_weight,
+                                         int rms_weight_dtype, const void* weight, const float* weight_scale,
+                                         void* out, void* residual_out, int64_t M, int64_t H, int64_t N, int64_t ldx,
+                                         int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro, float eps, int dtype,
+                                         int flags, void* stream) {
+  if (!weight || !weight_scale) return fail(FQKV_ERR_NULL, "weight and weight_scale must be non-null");
+  // The rest is checked as fqkv_launch checks it, on the decode schedule; the one-byte
+  // weight's layout and aliasing are checked here.
+  Problem p{M, H, N, ldx, ldr, ldw, ldo, ldro, x, residual, rms_weight, nullptr, out, residual_out,
+            dtype, rms_weight_dtype, FQKV_SCHED_DECODE, flags, false};
+  if (int rc = validate(p)) return rc;
+  if (ldw < H) return fail(FQKV_ERR_SHAPE, "ldw %lld is smaller than H = %lld", (long long)ldw, (long long)H);
+  if (!aligned16(weight) || ldw % 16)
+    return fail(FQKV_ERR_ALIGN, "the e4m3 weight needs a 16-byte aligned address and a row pitch of 16-byte multiples");
+  if (reinterpret_cast<uintptr_t>(weight_scale) & 3u) return fail(FQKV_ERR_ALIGN, "weight_scale must be 4-byte aligned");
+  const int64_t wb = (N - 1) * ldw + H, sb = N * 4;
+  const int64_t ob = mat_bytes(M, N, ldo), rob = residual_out ? mat_bytes(M, H, ldro) : 0;
+  if (overlaps(out, ob, weight, wb) || overlaps(out, ob, weight_scale, sb) || overlaps(residual_out, rob, weight, wb) ||
+      overlaps(residual_out, rob, weight_scale, sb))
+    return fail(FQKV_ERR_ALIAS, "out or residual_out overlaps the weight or its scale");
+  DeviceInfo d;
+  if (int rc = device_info(&d)) return rc;
+  if (d.major != 10) return fail(FQKV_ERR_DEVICE, "compute capability %d.%d is not sm_100", d.major, d.minor);
+  DecodeConfig c;
+  if (decode_pick_config((int)M, (int)H, (int)N, d.sms, &c, true))
+    return fail(FQKV_ERR_SCHEDULE,
+                "no fused decode configuration takes M = %lld, H = %lld, N = %lld with e4m3 weights (M <= 64)",
+                (long long)M, (long long)H, (long long)N);
+  CUtensorMap tmW;
+  if (int rc = make_map(&tmW, weight, N, H, ldw, 128 * decode_box_tiles(c.nt), kMapE4M3)) return rc;
+  DecodeParams dp{static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(residual), rms_weight,
+                  rms_weight_dtype, static_cast<uint16_t*>(out), static_cast<uint16_t*>(residual_out), (int)M,
+                  (int)H, (int)N, ldx, ldr, ldo, ldro, eps, (int)((H + 63) / 64), 0, flags, 0, 0, weight_scale};
+  dp.nkb_max = (dp.kb_total + c.cluster - 1) / c.cluster;
+  // Rings of two stages skip programmatic dependent launch (as on the 16-bit path; here at
+  // every M: the N = 28672 configuration measured 65.9 us at M = 1 with it).
+  const bool pdl = (flags & FQKV_FLAG_PDL) != 0 && c.stages > 2;
+  const cudaError_t e = launch_decode(c, tmW, dp, dtype == FQKV_BF16, pdl, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? 0 : cuda_fail(e, "decode kernel launch (e4m3 weights)");
+}
+
 extern "C" FQKV_API int fqkv_rope_split(const void* qkv, int64_t ldq, const void* cos, const void* sin,
                                         int64_t cos_batch, void* q, void* k, void* v, int64_t B, int64_t S,
                                         int n_q_heads, int n_kv_heads, int head_dim, int dtype, void* stream) {
@@ -457,7 +509,7 @@ extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const v
     if (int rc = make_map(&tmW, weight, N, H, ldw, 128 * decode_box_tiles(c.nt), bf16)) return rc;
     DecodeParams dp{xs, rs, rms_weight, rms_weight_dtype, static_cast<uint16_t*>(out),
                     static_cast<uint16_t*>(residual_out), (int)M, (int)H, (int)N, ldx, ldr, ldo, ldro, eps,
-                    (int)((H + 63) / 64), 0, flags};
+                    (int)((H + 63) / 64), 0, flags, 0, 0, nullptr};
     dp.nkb_max = (dp.kb_total + c.cluster - 1) / c.cluster;
     // A ring of two stages (the wide-weight configurations, 64-80 KB stages) is filled
     // entirely by the stages issued ahead of the preceding grid, and then the stream

@@ -33,6 +33,8 @@
 #include <tuple>
 #include <type_traits>
 
+#include <cuda_fp8.h>
+
 #include "fqkv_kernels.cuh"
 
 namespace fqkv {
@@ -46,6 +48,13 @@ constexpr int kMaxCluster = 8;
 constexpr int kTileRows = 128;      // rows of W per MMA (UMMA M)
 constexpr int kKBlock = 64;         // K elements per stage (128 bytes of 16-bit data)
 constexpr int kWTileBytes = kTileRows * 128;
+// e4m3 weights: a ring tile is 128 rows of 128 one-byte elements (two 64-deep k-blocks, one
+// full 128-byte line per row), as many bytes as a 16-bit tile.
+constexpr int kW8Row = 128;
+// e4m3 weights: converted 16-bit A tiles in flight, in TMEM after the accumulators (32
+// columns each: 128 rows x 64 values): at most 5 * 32 + 8 * 32 = 416 of 512 columns.
+constexpr int kConvSlots = 8;
+__host__ __device__ constexpr int a_col_base(int nt, int mpad) { return (nt * mpad + 31) / 32 * 32; }
 constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
 constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
 
@@ -53,31 +62,85 @@ struct Layout {
   uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, bars, tmem_slot, total;
 };
 
-__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max) {
+// f8: the ring holds e4m3 tiles (128-byte rows of two k-blocks, 128-byte swizzle); the
+// converted tiles live in TMEM.
+__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max, bool f8 = false) {
   Layout L;
   L.stage_bytes = nt * kWTileBytes;
   L.ring = 0;
-  L.normed = L.ring + stages * L.stage_bytes;
+  L.normed = L.ring + stages * L.stage_bytes;  // 1024-aligned: stages are multiples of 16 KB
   L.gain = L.normed + (uint32_t)nkb_max * mpad * 128;  // [nkb_max * 64] fp32 gain slice
   L.red = L.gain + (uint32_t)nkb_max * kKBlock * 4;    // [kMaxCluster][mpad] floats
   L.rowp = L.red + kMaxCluster * mpad * 4;            // [mpad] floats
   L.rstd = L.rowp + mpad * 4;                         // [mpad] floats
   L.bars = (L.rstd + mpad * 4 + 7) & ~7u;   // full[S], empty[S], accum, normed, sum, part, acts, recv
-  L.tmem_slot = L.bars + (2 * stages + 6) * 8;
+  L.tmem_slot = L.bars + (2 * stages + 6 + (f8 ? 2 * kConvSlots : 0)) * 8;  // + cfull, cempty
   L.total = L.tmem_slot + 16;
   return L;
+}
+
+// Two e4m3 values -- bytes 0 and 1 of `w` (sel 0x1404) or bytes 2 and 3 (sel 0x3424) -- as
+// two values of the dtype, the lower byte in the lower half.  The byte permute places each
+// byte in the high byte of its 16-bit half; the shift puts the e4m3 exponent and mantissa
+// bits into the low end of the target's exponent field and the top of its mantissa (the
+// sign stays at bit 15), and the packed multiply by 2^(target bias - 7) -- 2^120 for bf16,
+// 2^8 for fp16 -- rescales.  Normal and subnormal e4m3 values come out exact (an e4m3
+// subnormal becomes a subnormal of the target before the multiply).  The e4m3fn NaN
+// encodings are read as +-480; quantize_weight_e4m3 never produces them.
+template <typename T>
+__device__ __forceinline__ uint32_t e4m3x2_to(uint32_t w, uint32_t sel);
+template <>
+__device__ __forceinline__ uint32_t e4m3x2_to<__half>(uint32_t w, uint32_t sel) {
+  const uint32_t x = __byte_perm(w, 0u, sel);
+  const uint32_t bits = (x & 0x80008000u) | ((x >> 1) & 0x3F803F80u);
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(0x5C005C00u));  // 2^8
+  return r;
+}
+template <>
+__device__ __forceinline__ uint32_t e4m3x2_to<__nv_bfloat16>(uint32_t w, uint32_t sel) {
+  const uint32_t x = __byte_perm(w, 0u, sel);
+  const uint32_t bits = (x & 0x80008000u) | ((x >> 4) & 0x07F007F0u);
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(0x7B807B80u));  // 2^120
+  return r;
+}
+
+// A warp's share of one 128 x 64 k-block of e4m3 weights, converted into TMEM: rows
+// 32q .. 32q + 31 (q = warp % 4, the lane quadrant the warp may access; lane = row) and
+// values 32 hf .. 32 hf + 31 of the k-block (hf = which of the quadrant's two warps).  The
+// ring row is 128 bytes (two k-blocks, 128-byte swizzle: 16-byte chunk j at j ^ (row % 8)),
+// `h` picks the k-block.  Each lane converts its 32 values into 16 columns of the A slot.
+template <typename T>
+__device__ __forceinline__ void convert_w8_to_tmem(const uint8_t* tile, int h, int q, int hf, int lane,
+                                                   uint32_t a_taddr) {
+  const int r = q * 32 + lane;
+  const uint8_t* row = tile + r * kW8Row;
+  uint32_t o[16];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int j = 4 * h + 2 * hf + u;  // logical 16-byte chunk of the row
+    const uint4 raw = *reinterpret_cast<const uint4*>(row + ((j ^ (r & 7)) << 4));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      o[8 * u + 2 * v] = e4m3x2_to<T>(w[v], 0x1404u);
+      o[8 * u + 2 * v + 1] = e4m3x2_to<T>(w[v], 0x3424u);
+    }
+  }
+  tmem_st16(a_taddr + ((uint32_t)(q * 32) << 16) + 16 * hf, o);
 }
 
 __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
 }
 
-template <typename T, int MPAD, int NT>
+template <typename T, int MPAD, int NT, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmW, const DecodeParams p, const int stages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = make_layout(stages, NT, MPAD, p.nkb_max);
+  const Layout L = make_layout(stages, NT, MPAD, p.nkb_max, F8);
   uint8_t* ring = smem + L.ring;
   uint8_t* normed = smem + L.normed;
   float* red = reinterpret_cast<float*>(smem + L.red);
@@ -91,6 +154,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* part_bar = accum_bar + 3;  // every CTA of the cluster has written its partial tile
   uint64_t* acts_bar = accum_bar + 4;  // the norm warps have issued their activation loads
   uint64_t* recv_bar = accum_bar + 5;  // the peers' slices of this CTA's share have landed
+  uint64_t* cfull = accum_bar + 6;     // e4m3 weights: conversion slot filled (8 warps)
+  uint64_t* cempty = cfull + kConvSlots;  // e4m3 weights: conversion slot consumed (MMA commit)
   float* gain_s = reinterpret_cast<float*>(smem + L.gain);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   // The epilogue reuses buffers the MMAs no longer need: this CTA's partial tile
@@ -108,14 +173,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb0 = (int)((rank * (uint32_t)KB) / C), kb1 = (int)(((rank + 1) * (uint32_t)KB) / C);
   const int nkb = kb1 - kb0;
   const int n_base = blockIdx.y * NT * kTileRows;
-  constexpr uint32_t kTmemCols = tmem_cols_for(NT * MPAD);
+  // Accumulators [0, NT * MPAD); e4m3 weights: kConvSlots A tiles of 32 columns after them.
+  constexpr uint32_t kACol = a_col_base(NT, MPAD);
+  constexpr uint32_t kTmemCols = tmem_cols_for(F8 ? kACol + kConvSlots * 32 : NT * MPAD);
   constexpr int kBoxTiles = decode_box_tiles(NT);
 
   // ---------------------------------------------------------------- setup
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], F8 ? kNormWarps : 1);  // e4m3: freed by the converting warps
+    }
+    if (F8) {
+      for (int i = 0; i < kConvSlots; ++i) {
+        mbar_init(&cfull[i], kNormWarps);
+        mbar_init(&cempty[i], 1);
+      }
     }
     mbar_init(accum_bar, 1);
     mbar_init(normed_bar, 1);
@@ -145,11 +218,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // norm warps have requested their activations, so those small, latency-critical
       // loads are not queued behind megabytes of weight in the memory system.
       if (!(p.flags & FQKV_FLAG_STATIC_WEIGHTS)) pdl_wait();
-      const int pre = min(nkb, min(stages, p.pre_stages));
+      const int pre = min(F8 ? (nkb + 1) / 2 : nkb, min(stages, p.pre_stages));
       const uint64_t pol_w = policy_evict_first();
       bool ok = true;
       int s = 0, round = 0, issued = 0;
-      for (int i = 0; i < nkb; ++i) {
+      const int nstage = F8 ? (nkb + 1) / 2 : nkb;  // e4m3: a ring stage holds two k-blocks
+      for (int i = 0; i < nstage; ++i) {
         if (i == pre) ok = mbar_wait(acts_bar, 0);
         if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
         mbar_arrive_expect_tx(&full[s], tx);
@@ -157,8 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // boxes of 128 rows (a TMA box dimension is at most 256).
 #pragma unroll
         for (int j = 0; j < NT; j += kBoxTiles)
-          tma_load_2d_hint(ring + s * L.stage_bytes + j * kWTileBytes, &tmW, &full[s], (kb0 + i) * kKBlock,
-                           n_base + j * kTileRows, pol_w);
+          tma_load_2d_hint(ring + s * L.stage_bytes + j * kWTileBytes, &tmW, &full[s],
+                           (kb0 + (F8 ? 2 * i : i)) * kKBlock, n_base + j * kTileRows, pol_w);
         ++issued;
         if (++s == stages) {
           s = 0;
@@ -176,7 +250,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = make_idesc_f16(kTileRows, MPAD, std::is_same<T, __nv_bfloat16>::value);
       bool ok = mbar_wait(normed_bar, 0);
       int s = 0, round = 0;
-      for (int i = 0; i < nkb && ok; ++i) {
+      if (F8) {
+        // e4m3 weights: each 128-row tile arrives converted in a slot of its own.
+        for (int i = 0; i < nkb && ok; ++i) {
+          const uint32_t b_base = smem_u32(normed + i * MPAD * 128);
+#pragma unroll 1
+          for (int nt = 0; nt < NT; ++nt) {
+            const int task = i * NT + nt, slot = task % kConvSlots;
+            if (!(ok = mbar_spin(&cfull[slot], (task / kConvSlots) & 1))) break;
+            tc_fence_after();
+            const uint32_t a_tmem = tmem_base + kACol + slot * 32;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_f16_ts(tmem_base + nt * MPAD, a_tmem + kk * 8, make_sw128_desc(b_base + kk * 32), idesc,
+                          (i > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&cempty[slot]);
+          }
+        }
+      }
+      for (int i = 0; i < (F8 ? 0 : nkb) && ok; ++i) {
         if (!(ok = mbar_wait(&full[s], round & 1))) break;
         tc_fence_after();
         const uint32_t a_base = smem_u32(ring + s * L.stage_bytes);
@@ -384,6 +476,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("bar.sync 1, 256;" ::: "memory");
     if (et == 0) mbar_arrive(normed_bar);
 
+    if (F8) {
+      // e4m3 weights: convert stage s of the ring tile by tile into the conversion slots
+      // the MMA reads.  Each warp converts its rows of every tile and waits on its own (no
+      // named barrier in this loop: a warp whose bounded wait gives up leaves early, and
+      // every warp still meets the epilogue's barriers the same number of times).
+      bool wok = ok;
+      for (int js = 0; 2 * js < nkb && wok; ++js) {  // ring stage js: k-blocks 2 js, 2 js + 1
+        const int s = js % stages;
+        wok = __all_sync(0xffffffffu, mbar_wait(&full[s], (js / stages) & 1));
+        for (int h = 0; h < 2 && 2 * js + h < nkb && wok; ++h) {
+          const int i = 2 * js + h;
+          for (int nt = 0; nt < NT && wok; ++nt) {
+            const int task = i * NT + nt, slot = task % kConvSlots;
+            if (task >= kConvSlots)
+              wok = __all_sync(0xffffffffu, mbar_spin(&cempty[slot], (task / kConvSlots - 1) & 1));
+            if (!wok) break;
+            convert_w8_to_tmem<T>(ring + s * L.stage_bytes + nt * kWTileBytes, h, warp & 3, (warp - 2) >> 2, lane,
+                                  tmem_base + kACol + slot * 32);
+            tmem_wait_st();
+            tc_fence_before();  // the MMA thread reads the slot after the arrive below
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&cfull[slot]);
+          }
+        }
+        __syncwarp();
+        if (wok && lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
+      }
+      ok = bar_and(1, kNormThreads, wok) && ok;  // every warp has left the loop
+    }
+
     // Epilogue: TMEM -> registers -> this CTA's partial tile in shared memory, laid out
     // [m][nt][row] so that every rank's share is one contiguous byte range.
     ok = mbar_wait(accum_bar, 0) && ok;
@@ -445,6 +567,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t mn = f / (kTileRows / 4);
       const int nt = (int)(mn % NT), m = (int)(mn / NT);
       const int n = n_base + nt * kTileRows + nl;
+      if (F8) {  // e4m3 weights: the row scale, once, on the k-summed value
+        acc.x *= n < p.N ? p.wscale[n] : 0.f;
+        acc.y *= n + 1 < p.N ? p.wscale[n + 1] : 0.f;
+        acc.z *= n + 2 < p.N ? p.wscale[n + 2] : 0.f;
+        acc.w *= n + 3 < p.N ? p.wscale[n + 3] : 0.f;
+      }
       uint16_t* dst = p.out + (int64_t)m * p.ldo + n;
       if (vec_store && n + 3 < p.N) {
         *reinterpret_cast<uint2*>(dst) = make_uint2(Elem<T>::from_f2(acc.x, acc.y), Elem<T>::from_f2(acc.z, acc.w));
@@ -473,9 +601,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int MPAD, int NT>
+template <int MPAD, int NT, bool F8>
 auto kernel_ptr(bool bf16) {
-  return bf16 ? decode_kernel<__nv_bfloat16, MPAD, NT> : decode_kernel<__half, MPAD, NT>;
+  return bf16 ? decode_kernel<__nv_bfloat16, MPAD, NT, F8> : decode_kernel<__half, MPAD, NT, F8>;
 }
 
 using KernelFn = void (*)(CUtensorMap, DecodeParams, int);
@@ -484,17 +612,22 @@ using KernelFn = void (*)(CUtensorMap, DecodeParams, int);
 // for MPAD 16 and 32.
 constexpr int kMaxNT = 5;
 
-KernelFn pick_kernel(int mpad, int nt, bool bf16) {
+template <bool F8>
+KernelFn pick_kernel_t(int mpad, int nt, bool bf16) {
   switch (nt) {
-    case 1: return mpad == 16 ? kernel_ptr<16, 1>(bf16) : mpad == 32 ? kernel_ptr<32, 1>(bf16)
-                 : mpad == 64 ? kernel_ptr<64, 1>(bf16) : nullptr;
-    case 2: return mpad == 16 ? kernel_ptr<16, 2>(bf16) : mpad == 32 ? kernel_ptr<32, 2>(bf16)
-                 : mpad == 64 ? kernel_ptr<64, 2>(bf16) : nullptr;
-    case 3: return mpad == 16 ? kernel_ptr<16, 3>(bf16) : mpad == 32 ? kernel_ptr<32, 3>(bf16) : nullptr;
-    case 4: return mpad == 16 ? kernel_ptr<16, 4>(bf16) : mpad == 32 ? kernel_ptr<32, 4>(bf16) : nullptr;
-    case 5: return mpad == 16 ? kernel_ptr<16, 5>(bf16) : mpad == 32 ? kernel_ptr<32, 5>(bf16) : nullptr;
+    case 1: return mpad == 16 ? kernel_ptr<16, 1, F8>(bf16) : mpad == 32 ? kernel_ptr<32, 1, F8>(bf16)
+                 : mpad == 64 ? kernel_ptr<64, 1, F8>(bf16) : nullptr;
+    case 2: return mpad == 16 ? kernel_ptr<16, 2, F8>(bf16) : mpad == 32 ? kernel_ptr<32, 2, F8>(bf16)
+                 : mpad == 64 ? kernel_ptr<64, 2, F8>(bf16) : nullptr;
+    case 3: return mpad == 16 ? kernel_ptr<16, 3, F8>(bf16) : mpad == 32 ? kernel_ptr<32, 3, F8>(bf16) : nullptr;
+    case 4: return mpad == 16 ? kernel_ptr<16, 4, F8>(bf16) : mpad == 32 ? kernel_ptr<32, 4, F8>(bf16) : nullptr;
+    case 5: return mpad == 16 ? kernel_ptr<16, 5, F8>(bf16) : mpad == 32 ? kernel_ptr<32, 5, F8>(bf16) : nullptr;
     default: return nullptr;
   }
+}
+
+KernelFn pick_kernel(int mpad, int nt, bool bf16, bool f8) {
+  return f8 ? pick_kernel_t<true>(mpad, nt, bf16) : pick_kernel_t<false>(mpad, nt, bf16);
 }
 
 cudaLaunchConfig_t base_config(const DecodeConfig& c, int tiles, cudaLaunchAttribute* attr, int* na) {
@@ -515,16 +648,16 @@ cudaLaunchConfig_t base_config(const DecodeConfig& c, int tiles, cudaLaunchAttri
 // How many clusters of this configuration the device keeps resident at once (cached).
 int max_active_clusters(const DecodeConfig& c, int tiles) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int, size_t>, int> cache;
+  static std::map<std::tuple<int, int, int, int, size_t, int>, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, c.mpad, c.nt, c.cluster, c.smem);
+  const auto key = std::make_tuple(dev, c.mpad, c.nt, c.cluster, c.smem, c.f8);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  KernelFn k = pick_kernel(c.mpad, c.nt, true);
+  KernelFn k = pick_kernel(c.mpad, c.nt, true, c.f8 != 0);
   int n = 0;
   if (k && ensure_smem_attr(reinterpret_cast<const void*>(k), c.smem) == cudaSuccess) {
     cudaLaunchAttribute attr[2];
@@ -549,14 +682,14 @@ constexpr size_t kSmemLimit = 232448;  // max dynamic shared memory per block on
 
 size_t decode_smem_bytes(const DecodeConfig& c, int kb_total) {
   const int nkb_max = (kb_total + c.cluster - 1) / c.cluster;
-  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max).total;
+  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8 != 0).total;
 }
 
 // Choose (tile rows, cluster size, ring depth).  Candidates must fit shared memory and
 // have every cluster resident at once; among them the one using the most SMs wins (ties
 // go to the deeper ring, then to the smaller cluster).
 // FQKV_DECODE_NT / FQKV_DECODE_CLUSTER / FQKV_DECODE_STAGES restrict the search.
-int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
+int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, bool f8) {
   const int mpad = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
   if (mpad == 0) return FQKV_ERR_SCHEDULE;
   // Tuning overrides, read once per process.
@@ -566,10 +699,10 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
   // The search below queries occupancy for many candidates; its result is cached per
   // (device, MPAD, H, N, SM count, overrides), so a model's per-step calls skip it.
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int, int, int, int, int>, std::pair<int, DecodeConfig>> cache;
+  static std::map<std::tuple<int, int, int, int, int, int, int, int, int>, std::pair<int, DecodeConfig>> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, mpad, H, N, sm_count, force_nt, force_c, force_s);
+  const auto key = std::make_tuple(dev, mpad, H, N, sm_count, force_nt, force_c, force_s, f8 ? 1 : 0);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -583,7 +716,8 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
   long best_score = -1;
   for (int nt = 1; nt <= kMaxNT; ++nt) {
     if (force_nt && nt != force_nt) continue;
-    if (!pick_kernel(mpad, nt, true)) continue;
+    if (!pick_kernel(mpad, nt, true, f8)) continue;
+    const int tile_bytes = kWTileBytes;  // one 128-row tile in the ring (e4m3: two k-blocks)
     const int tiles = (N + nt * kTileRows - 1) / (nt * kTileRows);
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
@@ -594,10 +728,10 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
       const int recv_bytes = cl * 16 * ((nt * mpad * (kTileRows / 4) + cl - 1) / cl);
       const int recv_in_normed = recv_bytes <= (KB + cl - 1) / cl * mpad * 128 ? 1 : 0;
       const int epi_bytes = part_bytes + (recv_in_normed ? 0 : recv_bytes);
-      const int min_stages = (epi_bytes + nt * kWTileBytes - 1) / (nt * kWTileBytes);
+      const int min_stages = (epi_bytes + nt * tile_bytes - 1) / (nt * tile_bytes);
       for (int st = 16; st >= max(2, min_stages); --st) {
         if (force_s && st != force_s) continue;
-        DecodeConfig t{mpad, nt, st, cl, 0, recv_in_normed};
+        DecodeConfig t{mpad, nt, st, cl, 0, recv_in_normed, f8 ? 1 : 0};
         t.smem = decode_smem_bytes(t, KB);
         if (t.smem > kSmemLimit) continue;
         const int resident = max_active_clusters(t, tiles);
@@ -622,7 +756,7 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
 
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream) {
-  KernelFn k = pick_kernel(c.mpad, c.nt, bf16);
+  KernelFn k = pick_kernel(c.mpad, c.nt, bf16, c.f8 != 0);
   if (!k) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(k), c.smem);
   if (e != cudaSuccess) return e;

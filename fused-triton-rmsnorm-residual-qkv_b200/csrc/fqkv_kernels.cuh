@@ -66,6 +66,7 @@ struct DecodeParams {
   int pre_stages;     // weight stages issued before the activation loads are out
   int recv_in_normed; // the epilogue's receive slots use the (then idle) normalised-activation
                       // buffer instead of the ring
+  const float* wscale;  // e4m3 weights: fp32 scale per weight row (output feature); else null
 };
 
 struct StreamKParams {
@@ -318,14 +319,15 @@ constexpr int kDecodeThreads = 64 + 8 * 32;
 
 struct DecodeConfig {
   int mpad;     // token columns of the MMA (16, 32 or 64)
-  int nt;       // 128-row W tiles per CTA (1 or 2)
+  int nt;       // 128-row W tiles per CTA (1 to 5)
   int stages;   // ring depth
   int cluster;  // CTAs splitting K (cluster size)
   size_t smem;  // dynamic shared memory bytes
   int recv_in_normed;  // see DecodeParams
+  int f8;       // e4m3 weights (converted to the dtype in shared memory before the MMA)
 };
 
-int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg);
+int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, bool f8 = false);
 // 128-row weight tiles per TMA box of the decode kernel's weight map: one box per stage
 // for NT <= 2, else NT boxes of 128 rows (a box dimension is at most 256 elements).
 __host__ __device__ constexpr int decode_box_tiles(int nt) { return nt <= 2 ? nt : 1; }

@@ -32,6 +32,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libfqkv.so"
 EXPORTED_SYMBOLS = (
     "fqkv_launch",
     "fqkv_launch_noalloc",
+    "fqkv_launch_fp8w",
     "fqkv_rope_split",
     "fqkv_workspace_bytes",
     "fqkv_query_schedule",
@@ -80,6 +81,9 @@ def load() -> ctypes.CDLL:
     lib.fqkv_device_status.restype = i32
     lib.fqkv_version.argtypes = []
     lib.fqkv_version.restype = i32
+    lib.fqkv_launch_fp8w.argtypes = [vp, vp, vp, i32, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, f32,
+                                     i32, i32, vp]
+    lib.fqkv_launch_fp8w.restype = i32
     lib.fqkv_rope_split.argtypes = [vp, i64, vp, vp, i64, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp]
     lib.fqkv_rope_split.restype = i32
     _lib = lib
@@ -106,6 +110,12 @@ def launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx,
            dtype, schedule, flags, ws_ptr, ws_bytes, stream) -> int:
     return load().fqkv_launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw,
                               ldo, ldro, ctypes.c_float(eps), dtype, schedule, flags, ws_ptr, ws_bytes, stream)
+
+
+def launch_fp8w(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, scale_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw, ldo,
+                ldro, eps, dtype, flags, stream) -> int:
+    return load().fqkv_launch_fp8w(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, scale_ptr, out_ptr, rout_ptr, M, H, N, ldx,
+                                   ldr, ldw, ldo, ldro, ctypes.c_float(eps), dtype, flags, stream)
 
 
 def rope_split(qkv_ptr, ldq, cos_ptr, sin_ptr, cos_batch, q_ptr, k_ptr, v_ptr, B, S, n_q, n_kv, head_dim,

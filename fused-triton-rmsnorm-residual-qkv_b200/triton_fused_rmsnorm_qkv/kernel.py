@@ -239,6 +239,86 @@ def fused_rmsnorm_residual_qkv(
     return q, k, v
 
 
+E4M3_MAX = 448.0  # largest finite float8_e4m3fn value
+
+
+def quantize_weight_e4m3(weight: torch.Tensor):
+    """(w8, scale): ``weight`` (N, H) as float8_e4m3fn with one fp32 scale per row,
+    ``scale[n] = max_k |weight[n, k]| / 448`` (1 for an all-zero row), ``w8 = weight / scale``
+    rounded to e4m3.  ``w8.float() * scale[:, None]`` approximates ``weight``."""
+    if weight.dim() != 2:
+        raise ValueError(f"weight must be (N, H), got shape {tuple(weight.shape)}")
+    w = weight.float()
+    amax = w.abs().amax(dim=1)
+    scale = torch.where(amax > 0, amax / E4M3_MAX, torch.ones_like(amax))
+    w8 = (w / scale[:, None]).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn)
+    return w8.contiguous(), scale.contiguous()
+
+
+def fused_add_rmsnorm_matmul_fp8w(
+    x: torch.Tensor,
+    residual: Optional[torch.Tensor],
+    rms_weight: torch.Tensor,
+    weight_e4m3: torch.Tensor,
+    weight_scale: torch.Tensor,
+    eps: float = 1e-6,
+    *,
+    return_residual: bool = True,
+    static_weights: Optional[bool] = None,
+):
+    """``fused_add_rmsnorm_matmul`` with an FP8 (e4m3) weight and an fp32 scale per weight row.
+
+    ``out = dtype(weight_scale[n] * sum_k normed[m, k] * weight_e4m3[n, k])`` with ``normed``
+    exactly as the 16-bit path forms it (``quantize_weight_e4m3`` makes the pair from a 16-bit
+    weight).  The fused decode kernel streams the one-byte weight -- half the bytes -- and
+    converts it exactly in shared memory before the tensor-core MMA.  Decode sizes only
+    (M = B * S <= 64); larger M raise ``ValueError``.
+    """
+    assert x.is_cuda, "Fused kernel requires CUDA tensors"
+    B, S, H = x.shape
+    if weight_e4m3.dtype != torch.float8_e4m3fn:
+        raise TypeError(f"weight_e4m3 must be torch.float8_e4m3fn, got {weight_e4m3.dtype}")
+    N = weight_e4m3.shape[0]
+    assert weight_e4m3.shape[1] == H, f"weight must be (N_OUT, H); got {weight_e4m3.shape} for H={H}"
+    if weight_scale.dtype != torch.float32 or weight_scale.numel() != N:
+        raise ValueError(f"weight_scale must be {N} float32 values, got {weight_scale.dtype} {tuple(weight_scale.shape)}")
+    if x.dtype not in _DTYPE_CODE:
+        raise TypeError(f"x must be float16 or bfloat16, got {x.dtype}")
+    if rms_weight.dtype not in _GAIN_CODE or rms_weight.numel() != H:
+        raise ValueError(f"rms_weight must hold H={H} float32/float16/bfloat16 values")
+    for name, t in (("residual", residual), ("rms_weight", rms_weight), ("weight_e4m3", weight_e4m3),
+                    ("weight_scale", weight_scale)):
+        if t is not None and t.device != x.device:
+            raise ValueError(f"{name} is on {t.device}, x is on {x.device}")
+    M = B * S
+    x2 = _rows(x, M, H)
+    r2 = None
+    if residual is not None:
+        if residual.numel() != M * H or residual.dtype != x.dtype:
+            raise ValueError(f"residual must match x {tuple(x.shape)} {x.dtype}")
+        r2 = _rows(residual, M, H)
+    w8 = weight_e4m3 if weight_e4m3.stride(1) == 1 else weight_e4m3.contiguous()
+    sc = weight_scale.reshape(N).contiguous()
+    g = rms_weight.reshape(H).contiguous()
+    out = torch.empty(B, S, N, dtype=x.dtype, device=x.device)
+    hidden = torch.empty_like(x) if return_residual else None
+    rout2 = _rows(hidden, M, H) if hidden is not None else None
+    if static_weights is None:
+        static_weights = _env_flag("FQKV_STATIC_WEIGHTS")
+    flags = _lib.FLAG_PDL | (_lib.FLAG_STATIC_WEIGHTS if static_weights else 0)
+    dev = x.device
+    ctx = contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
+    with ctx:
+        rc = _lib.launch_fp8w(
+            x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), _GAIN_CODE[g.dtype],
+            w8.data_ptr(), sc.data_ptr(), out.data_ptr(), rout2.data_ptr() if rout2 is not None else None,
+            M, H, N, _row_stride(x2), _row_stride(r2) if r2 is not None else 0, w8.stride(0), N,
+            _row_stride(rout2) if rout2 is not None else 0, float(eps), _DTYPE_CODE[x.dtype], flags,
+            _current_stream(dev.index))
+    _lib.check(rc, "fqkv_launch_fp8w")
+    return (out, hidden) if return_residual else out
+
+
 def qkv_rope_split(
     qkv: torch.Tensor,
     cos: torch.Tensor,

@@ -153,6 +153,24 @@ FQKV_API int fqkv_launch_noalloc(const void* x, const void* residual, const void
                 float eps, int dtype, int flags, void* stream);
 
 /*
+ * The op with an FP8 (e4m3) weight: out = dtype(scale[n] * sum_k normed[m, k] * w[n, k]),
+ * with normed formed exactly as fqkv_launch forms it.  The fused decode kernel streams the
+ * one-byte weight (half the bytes of a 16-bit weight) and converts it exactly to the dtype
+ * in shared memory before the tensor-core MMA; the fp32 row scale multiplies the k-summed
+ * value once.  No counterpart in the reference (FP8 weights are its README's future work).
+ *   weight        [N, H]  e4m3 (one byte per element), row stride ldw bytes; 16-byte aligned
+ *                 address and ldw a multiple of 16
+ *   weight_scale  [N]     fp32, 4-byte aligned
+ * Other arguments as fqkv_launch.  Runs the fused decode schedule only: M <= 64 and a
+ * configuration that fits the device, else FQKV_ERR_SCHEDULE.  Needs no workspace.
+ */
+FQKV_API int fqkv_launch_fp8w(const void* x, const void* residual, const void* rms_weight,
+                int rms_weight_dtype, const void* weight, const float* weight_scale, void* out,
+                void* residual_out, int64_t M, int64_t H, int64_t N,
+                int64_t ldx, int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro,
+                float eps, int dtype, int flags, void* stream);
+
+/*
  * Split the projection's output into head-major Q, K, V and rotate Q and K (rotary
  * position embedding), in one launch.  Replaces what the Llama integration does after
  * the fused call (llama3_patch.py:156-168): split by [n_q d, n_kv d, n_kv d], view as

@@ -17,3 +17,4 @@ from .rmsnorm_qkv import (  # noqa: F401
     within_bars,
 )
 from .rope import make_rope_case, rope_split  # noqa: F401,E402
+from .fp8w import forward_fp8w  # noqa: F401,E402

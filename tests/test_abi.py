@@ -149,3 +149,29 @@ def rope_call(**kw):
 def test_rope_split_rejects_before_any_cuda_call(kw, code):
     """fqkv_rope_split validates its arguments before touching the device."""
     assert rope_call(**kw) == code, _lib.last_error()
+
+
+def fp8_call(**kw):
+    a = dict(x=1 << 32, r=2 << 32, g=3 << 32, gdt=_lib.BF16, w=4 << 32, sc=5 << 32, out=6 << 32, rout=None,
+             M=4, H=256, N=512, ldx=256, ldr=256, ldw=256, ldo=512, ldro=256, eps=1e-5, dtype=_lib.BF16, flags=0,
+             stream=None)
+    a.update(kw)
+    return _lib.launch_fp8w(a["x"], a["r"], a["g"], a["gdt"], a["w"], a["sc"], a["out"], a["rout"], a["M"], a["H"],
+                            a["N"], a["ldx"], a["ldr"], a["ldw"], a["ldo"], a["ldro"], a["eps"], a["dtype"], a["flags"],
+                            a["stream"])
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(w=None), _lib.ERR_NULL),
+    (dict(sc=None), _lib.ERR_NULL),
+    (dict(x=None), _lib.ERR_NULL),
+    (dict(dtype=_lib.F32), _lib.ERR_DTYPE),
+    (dict(M=65), _lib.ERR_SCHEDULE),          # decode sizes only
+    (dict(ldw=255), _lib.ERR_SHAPE),
+    (dict(ldw=264), _lib.ERR_ALIGN),          # row pitch not a multiple of 16 bytes
+    (dict(w=(4 << 32) + 8), _lib.ERR_ALIGN),
+    (dict(sc=(5 << 32) + 2), _lib.ERR_ALIGN),
+    (dict(out=(4 << 32) + 1024), _lib.ERR_ALIAS),   # out inside the weight
+])
+def test_fp8w_rejects_before_any_cuda_call(kw, code):
+    assert fp8_call(**kw) == code, _lib.last_error()

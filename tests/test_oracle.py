@@ -98,3 +98,19 @@ def test_rope_oracle_matches_transformers(B, S, n_q, n_kv, d, cb, dtype):
     qr, kr = apply_rotary_pos_emb(qh, kh, cos.expand(B, S, d), sin.expand(B, S, d))
     assert torch.equal(q, qr) and torch.equal(k, kr)
     assert torch.equal(v, vs.reshape(B, S, n_kv, d).transpose(1, 2))
+
+
+def test_e4m3_quantizer_round_trip_bound():
+    """quantize_weight_e4m3: w8 * scale is w to within e4m3's 3 mantissa bits (relative
+    2^-4 for normal values, 2^-10 * scale absolute below the normal range)."""
+    from triton_fused_rmsnorm_qkv import quantize_weight_e4m3
+
+    w = (0.02 * torch.randn(64, 256, generator=torch.Generator().manual_seed(4))).bfloat16()
+    w[3] = 0  # an all-zero row keeps scale 1
+    w8, scale = quantize_weight_e4m3(w)
+    assert w8.dtype == torch.float8_e4m3fn and scale.dtype == torch.float32 and scale[3] == 1
+    deq = w8.float() * scale[:, None]
+    err = (deq - w.float()).abs()
+    bound = torch.maximum(w.float().abs() * 2.0 ** -4, scale[:, None] * 2.0 ** -10)
+    assert bool((err <= bound).all())
+    assert torch.allclose(w8.float().abs().amax(dim=1)[w.float().abs().amax(dim=1) > 0], torch.tensor(448.0))
