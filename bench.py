@@ -23,7 +23,8 @@ residual add with the updated residual returned).  32 distinct seeded weight set
              Llama-3-70B M=1/16/256, the post-attention gate/up shape (N=28672), prefill
              M=512/2048/8192 (TFLOPS), the unfused PyTorch path (cuBLAS) on the same
              inputs as the GPU comparator, a streaming-read bandwidth for context, and
-             a 4-layer Llama-3-8B stack (M=1/16) unpatched vs the integration patch's
+             the FP8-weight path (e4m3 weight, Llama-3-8B decode M=1/16), and a
+             4-layer Llama-3-8B stack (M=1/16) unpatched vs the integration patch's
              modes (Q/K/V, + MLP gate/up, cross-layer, + one-launch Q/K/V rotary split).
 With N > 1 (torchrun) the layer is head-sharded column-parallel: each rank owns N/P
 weight rows and computes them with replicated inputs; no collective runs inside the
@@ -394,8 +395,37 @@ def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
             entry["speedup_vs_torch_unfused"] = round(t_ref / t_ms, 2)
         detail[label] = entry
         del ss
+    detail.update(run_fp8w_detail(dev, peaks))
     detail["llama3-8b_layer_stack"] = run_layer_stack(dev)
     return detail
+
+
+def run_fp8w_detail(dev, peaks: dict) -> dict:
+    """The FP8-weight path (e4m3 weight + fp32 row scale, quantize_weight_e4m3) on the
+    Llama-3-8B decode shape, graph-timed like the rows above.  Bytes: the one-byte weight
+    and its scales plus the 16-bit activations, gain, output and updated residual."""
+    from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul_fp8w, quantize_weight_e4m3
+
+    out = {}
+    wl = dict(WORKLOADS["llama3-8b-decode"], sets=32)
+    for mm in (1, 16):
+        ss, layout = make_sets(wl, mm, torch.bfloat16, dev, 1, 0, wl["sets"])
+        q8 = [(x, r, g, *quantize_weight_e4m3(w)) for (x, r, g, w) in ss]
+        del ss
+
+        def step(i):
+            x, r, g, w8, sc = q8[i % len(q8)]
+            fused_add_rmsnorm_matmul_fp8w(x, r, g, w8, sc, wl["eps"], static_weights=True)
+
+        t_ms = time_graph(step, 2000, 5, dev) / 2000
+        H, N = wl["H"], layout.n_out
+        b = N * H + 4 * N + algorithmic_bytes(mm, H, 0, True) + 2 * mm * N  # + the output
+        out[f"llama3-8b_decode_fp8w_M{mm}"] = {
+            "M": mm, "H": H, "N": N, "dtype": "bf16 activations, e4m3 weight", "us": round(t_ms * 1e3, 3),
+            "GB/s": round(b / t_ms / 1e6, 1), "pct_of_measured_hbm": round(100 * b / t_ms / 1e6 / peaks["hbm_gbs"], 2)}
+        del q8
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_layer_stack(dev, n_layers: int = 4, ms=(1, 16), steps: int = 50) -> dict:
