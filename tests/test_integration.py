@@ -85,6 +85,14 @@ def test_cross_layer_patch_bookkeeping():
     assert not any(hasattr(layer, "_fused_carry") for layer in model.model.layers)
 
 
+def test_rope_patch_bookkeeping():
+    model = tiny_llama()
+    with fused_patch(model, rope=True):
+        assert all(getattr(layer, "_fused_rope", False) for layer in model.model.layers)
+        assert not any(hasattr(layer, "_fused_packed_gate_up") for layer in model.model.layers)
+    assert not any(hasattr(layer, "_fused_rope") for layer in model.model.layers)
+
+
 def test_llama3_8b_config_shape():
     assert LLAMA3_8B_CONFIG["hidden_size"] + 2 * LLAMA3_8B_CONFIG["num_key_value_heads"] * \
         LLAMA3_8B_CONFIG["head_dim"] == 6144
