@@ -8,21 +8,25 @@
 //
 // Grid = (C, n_tiles), cluster = (C, 1, 1).  CTA `rank` of a cluster owns the
 // contiguous K slice [kb0, kb1) (64-element k-blocks) of n-tile blockIdx.y (NT x 128
-// weight rows).  Warp roles (192 threads):
+// weight rows, NT = 1 .. 5).  Warp roles (320 threads):
 //   warp 0     TMA producer: streams the CTA's weight slice through a STAGES-deep
-//              ring of 128B-swizzled tiles (one TMA load per stage, no multicast).
+//              ring of 128B-swizzled tiles (no multicast).
 //   warp 1     TMEM allocator and single-thread MMA issuer (tcgen05.mma kind::f16,
 //              fp32 accumulators in TMEM, tcgen05.commit frees ring stages).
-//   warps 2-5  norm + epilogue.  Read x (+ residual) for the slice, form
+//   warps 2-9  norm + epilogue.  Read x (+ residual) for the slice, form
 //              h = dtype(x + r) (bit-exact, baseline.py:48), write the updated residual
 //              (n-tile 0 only), keep h in shared memory in the UMMA operand layout,
 //              exchange per-row partial sums of squares across the cluster through
 //              DSMEM, then normalise in place: dtype((h * rstd) * g) (baseline.py:59-62).
 //              The normalised activations never leave shared memory.
 //              Epilogue: TMEM -> registers -> shared memory; each CTA bulk-copies
-//              the slice of its partial tile that rank o owns into rank o's idle ring
+//              the slice of its partial tile that rank o owns into rank o's idle buffers
 //              (cp.async.bulk shared::cta -> shared::cluster), and each owner sums the C
 //              partials of its slice in rank order (deterministic) and stores it.
+// F8 variant (e4m3 weights with an fp32 scale per row): the ring holds 128-byte e4m3
+// rows (two k-blocks), warps 2-9 convert each k-block exactly to the 16-bit dtype
+// straight into TMEM (tcgen05.st), the MMA reads its A operand from TMEM, and the row
+// scale multiplies the k-summed value in the epilogue.
 // The host sizes (NT, C, STAGES) so that all clusters are resident at once
 // (cudaOccupancyMaxActiveClusters): a second wave would double the time.
 // Every wait is bounded (fqkv_device.cuh); after a timeout the kernel drains its own
