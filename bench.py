@@ -246,7 +246,9 @@ def op_step_fn(sets, eps, M, schedule=None):
 def launches_per_step(M: int, H: int, dtype_code: int) -> int:
     from triton_fused_rmsnorm_qkv import _lib
 
-    info = _lib.query_schedule(M, H, 6144, dtype_code)
+    from triton_fused_rmsnorm_qkv.kernel import schedule_info
+
+    info = schedule_info(M, H, 6144, {_lib.BF16: torch.bfloat16, _lib.F16: torch.float16}[dtype_code])
     return 2 if info["uses_prepass"] else 1
 
 
@@ -372,12 +374,13 @@ def hbm_read_peak_gbs(dev) -> float:
 
 def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
     from triton_fused_rmsnorm_qkv import _lib
+    from triton_fused_rmsnorm_qkv.kernel import schedule_info
 
     dtypes = {"bf16": (torch.bfloat16, _lib.BF16), "fp16": (torch.float16, _lib.F16)}
     detail = {"hbm_read_peak_gbs_torch_sum": round(hbm_read_peak_gbs(dev), 1)}
     for label, wname, mm, dname, res, n_sets, comparator in DETAIL:
         wl = dict(WORKLOADS[wname], res=res, sets=n_sets)
-        dt, dcode = dtypes[dname]
+        dt, _ = dtypes[dname]
         ss, layout = make_sets(wl, mm, dt, dev, 1, 0, n_sets)
         H, N = wl["H"], layout.n_out
         k = 2000 if mm <= 64 else (200 if mm <= 512 else (40 if mm <= 2048 else 12))
@@ -388,7 +391,7 @@ def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
                  "GB/s": round(b / t_ms / 1e6, 1), "pct_of_measured_hbm": round(100 * b / t_ms / 1e6 / peaks["hbm_gbs"], 2),
                  "TFLOPS": round(fl / t_ms / 1e9, 1),
                  "pct_of_measured_bf16": round(100 * fl / t_ms / 1e9 / peaks["bf16_tflops"], 2),
-                 "schedule": _lib.SCHEDULE_NAMES[_lib.query_schedule(mm, H, N, dcode)["schedule"]]}
+                 "schedule": _lib.SCHEDULE_NAMES[schedule_info(mm, H, N, dt)["schedule"]]}
         if comparator:
             t_ref = time_graph(torch_step_fn(ss, wl["eps"]), k, 5, dev) / k
             entry["torch_unfused_us"] = round(t_ref * 1e3, 3)
@@ -522,7 +525,9 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
     value = job_bytes / step_s / 1e9
     from triton_fused_rmsnorm_qkv import _lib
 
-    sched = _lib.query_schedule(M, H, N_loc, _lib.BF16)
+    from triton_fused_rmsnorm_qkv.kernel import schedule_info
+
+    sched = schedule_info(M, H, N_loc)
     launches = args.steps * (2 if sched["uses_prepass"] else 1)
 
     # ---- verification of the sharded run (untimed): NCCL all-gather vs unsharded op

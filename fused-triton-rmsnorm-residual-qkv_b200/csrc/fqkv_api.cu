@@ -195,6 +195,7 @@ int64_t workspace_for(int sched, int64_t M, int64_t H, int64_t N) {
   if (sched == FQKV_SCHED_PREFILL) return align256(M * H * 2);
   if (sched == FQKV_SCHED_SPLIT)
     return align256(M * H * 2) + align256(streamk_partials_bytes((int)M)) + align256(streamk_counters_bytes((int)N));
+  if (sched == FQKV_SCHED_GRID) return align256(decode_grid_workspace_bytes(M, N));
   return 0;
 }
 
@@ -227,7 +228,7 @@ int validate(const Problem& p) {
     return fail(FQKV_ERR_SHAPE, "M, H and N must be below 2^31");
   if (p.ldx < p.H || p.ldw < p.H || p.ldo < p.N || (p.r && p.ldr < p.H) || (p.rout && p.ldro < p.H))
     return fail(FQKV_ERR_SHAPE, "a row stride is smaller than its row length");
-  if (p.schedule < FQKV_SCHED_AUTO || p.schedule > FQKV_SCHED_PREFILL)
+  if (p.schedule < FQKV_SCHED_AUTO || p.schedule > FQKV_SCHED_GRID)
     return fail(FQKV_ERR_SCHEDULE, "unknown schedule %d", p.schedule);
   if (p.flags & ~(FQKV_FLAG_PDL | FQKV_FLAG_STATIC_WEIGHTS))
     return fail(FQKV_ERR_SCHEDULE, "unknown flag bits 0x%x", p.flags);
@@ -249,6 +250,9 @@ int validate(const Problem& p) {
     if (sched == FQKV_SCHED_DECODE && p.M > kFusedMaxM)
       return fail(FQKV_ERR_SCHEDULE, "the decode schedule takes at most %lld rows (M = %lld)",
                   (long long)kFusedMaxM, (long long)p.M);
+    if (sched == FQKV_SCHED_GRID && (p.M > kGridMaxM || (p.N + 127) / 128 > kGridMaxTiles))
+      return fail(FQKV_ERR_SCHEDULE, "the grid schedule takes at most %d rows and %d output features "
+                  "(M = %lld, N = %lld)", kGridMaxM, kGridMaxTiles * 128, (long long)p.M, (long long)p.N);
     if (sched == FQKV_SCHED_SPLIT && p.M > kSplitMaxM)
       return fail(FQKV_ERR_SCHEDULE, "the split schedule takes at most %lld rows (M = %lld)",
                   (long long)kSplitMaxM, (long long)p.M);
@@ -284,7 +288,7 @@ cudaError_t ensure_smem_attr(const void* func, size_t bytes) {
 
 using namespace fqkv;
 
-extern "C" FQKV_API int fqkv_version(void) { return 101; }
+extern "C" FQKV_API int fqkv_version(void) { return 102; }
 
 // The projection's [M, (n_q + 2 n_kv) d] output to head-major Q, K, V with the rotary
 // embedding on Q and K (fqkv_rope.cu): what llama3_patch.py:156-168 does in PyTorch after
@@ -381,7 +385,7 @@ extern "C" FQKV_API const char* fqkv_last_error(void) { return t_last_error.c_st
 extern "C" FQKV_API int64_t fqkv_workspace_bytes(int64_t M, int64_t H, int64_t N, int dtype, int schedule) {
   if (M <= 0 || H <= 0 || N <= 0) return -fail(FQKV_ERR_SHAPE, "M, H and N must be positive");
   if (dtype != FQKV_F16 && dtype != FQKV_BF16) return -fail(FQKV_ERR_DTYPE, "unsupported dtype %d", dtype);
-  if (schedule < FQKV_SCHED_AUTO || schedule > FQKV_SCHED_PREFILL)
+  if (schedule < FQKV_SCHED_AUTO || schedule > FQKV_SCHED_GRID)
     return -fail(FQKV_ERR_SCHEDULE, "unknown schedule %d", schedule);
   DeviceInfo d;
   const int sched = schedule == FQKV_SCHED_AUTO ? auto_schedule_for(M, H, N, current_device_or_null(&d)) : schedule;
@@ -393,7 +397,7 @@ extern "C" FQKV_API int fqkv_query_schedule(int64_t M, int64_t H, int64_t N, int
   if (!info) return fail(FQKV_ERR_NULL, "info must be non-null");
   if (M <= 0 || H <= 0 || N <= 0) return fail(FQKV_ERR_SHAPE, "M, H and N must be positive");
   if (dtype != FQKV_F16 && dtype != FQKV_BF16) return fail(FQKV_ERR_DTYPE, "unsupported dtype %d", dtype);
-  if (schedule < FQKV_SCHED_AUTO || schedule > FQKV_SCHED_PREFILL)
+  if (schedule < FQKV_SCHED_AUTO || schedule > FQKV_SCHED_GRID)
     return fail(FQKV_ERR_SCHEDULE, "unknown schedule %d", schedule);
   DeviceInfo d;
   if (int rc = device_info(&d)) return rc;
@@ -414,6 +418,22 @@ extern "C" FQKV_API int fqkv_query_schedule(int64_t M, int64_t H, int64_t N, int
   if (sched == FQKV_SCHED_DECODE) {
     DecodeConfig c;
     if (int rc = decode_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
+    info->block_m = c.mpad;
+    info->block_n = 128 * c.nt;
+    info->block_k = 64;
+    info->stages = c.stages;
+    info->split_k = c.cluster;
+    info->grid = (int)(((N + 128 * c.nt - 1) / (128 * c.nt)) * c.cluster);
+    info->threads = kDecodeThreads;
+    info->smem_bytes = (int)c.smem;
+    info->uses_prepass = 0;
+    return 0;
+  }
+  if (sched == FQKV_SCHED_GRID) {
+    if (M > kGridMaxM) return fail(FQKV_ERR_SCHEDULE, "the grid schedule takes at most %d rows", kGridMaxM);
+    DecodeConfig c;
+    if (int rc = decode_grid_pick_config((int)M, (int)H, (int)N, d.sms, &c))
+      return fail(rc, "no grid configuration fits H=%lld N=%lld", (long long)H, (long long)N);
     info->block_m = c.mpad;
     info->block_n = 128 * c.nt;
     info->block_k = 64;
@@ -520,6 +540,23 @@ extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const v
     const bool decode_pdl = pdl && (c.stages > 2 || M == 1);
     e = launch_decode(c, tmW, dp, bf16, decode_pdl, st);
     return e == cudaSuccess ? 0 : cuda_fail(e, "decode kernel launch");
+  }
+
+  if (sched == FQKV_SCHED_GRID) {
+    DecodeConfig c;
+    if (int rc = decode_grid_pick_config((int)M, (int)H, (int)N, d.sms, &c))
+      return fail(rc, "no grid configuration fits H=%lld N=%lld", (long long)H, (long long)N);
+    CUtensorMap tmW;
+    if (int rc = make_map(&tmW, weight, N, H, ldw, 128 * decode_box_tiles(c.nt), bf16)) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    DecodeParams dp{xs, rs, rms_weight, rms_weight_dtype, static_cast<uint16_t*>(out),
+                    static_cast<uint16_t*>(residual_out), (int)M, (int)H, (int)N, ldx, ldr, ldo, ldro, eps,
+                    (int)((H + 63) / 64), 0, flags, 0, 0, nullptr,
+                    reinterpret_cast<float*>(ws + decode_grid_counter_bytes()),
+                    reinterpret_cast<int*>(ws)};
+    dp.nkb_max = (dp.kb_total + c.cluster - 1) / c.cluster;
+    e = launch_decode(c, tmW, dp, bf16, pdl && (c.stages > 2 || M == 1), st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "grid decode kernel launch");
   }
 
   // Pre-pass: updated residual + normalised rows (+ zeroed stream-K counters).

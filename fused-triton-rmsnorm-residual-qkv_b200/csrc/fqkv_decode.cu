@@ -31,6 +31,7 @@
 // (cudaOccupancyMaxActiveClusters): a second wave would double the time.
 // Every wait is bounded (fqkv_device.cuh); after a timeout the kernel drains its own
 // TMA loads and MMAs, frees TMEM and returns with the status word set.
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 #include <map>
@@ -60,6 +61,7 @@ constexpr int kW8Row = 128;
 constexpr int kConvSlots = 8;
 __host__ __device__ constexpr int a_col_base(int nt, int mpad) { return (nt * mpad + 31) / 32 * 32; }
 constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
+constexpr int kGridBatch = 8;       // grid variant: 16-byte chunks per thread loaded before any is used
 constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
 
 struct Layout {
@@ -139,7 +141,7 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
 }
 
-template <typename T, int MPAD, int NT, bool F8>
+template <typename T, int MPAD, int NT, bool F8, bool GRID>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmW, const DecodeParams p, const int stages) {
   extern __shared__ uint8_t smem_raw[];
@@ -171,8 +173,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* recv = p.recv_in_normed ? normed : ring + kPartBytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // C CTAs split K: the CTAs of a cluster, or (GRID) blockIdx.x of a row of independent CTAs.
   const uint32_t C = gridDim.x;
-  const uint32_t rank = cluster_ctarank();
+  const uint32_t rank = GRID ? blockIdx.x : cluster_ctarank();
+  static_assert(!(GRID && (F8 || MPAD != 16)), "the grid variant takes 16-bit weights and at most 16 rows");
+  static_assert(kNormWarps <= kMaxCluster, "the grid variant's per-warp row sums use the cluster sum slots");
   const int KB = p.kb_total;
   const int kb0 = (int)((rank * (uint32_t)KB) / C), kb1 = (int)(((rank + 1) * (uint32_t)KB) / C);
   const int nkb = kb1 - kb0;
@@ -324,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t slot_bytes = 16u * ((NT * MPAD * (kTileRows / 4) + C - 1) / C);
     // This CTA expects C * MPAD row sums (4 bytes each) from the cluster's st.async writes,
     // and later C - 1 bulk copies of its share of the tile.
-    if (et == 0) {
+    if (!GRID && et == 0) {
       mbar_arrive_expect_tx_cluster(sum_bar, C * MPAD * 4);
       mbar_arrive_expect_tx_cluster(recv_bar, (C - 1) * 16u * (share(rank + 1) - share(rank)));
     }
@@ -352,57 +357,118 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rows costs one memory latency (M = 16: one pair per warp).  When that is all of the
     // warp's work (MPAD = 16 and at most 32 * kLoadBatch chunks per row), h also stays in
     // registers for pass 2.
-    const bool h_in_regs = MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
+    const bool h_in_regs = !GRID && MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
     uint4 hkeep[2][kLoadBatch];
-    for (int m0 = nw; m0 < MPAD; m0 += 2 * kNormWarps) {
-      uint64_t ss2[2] = {0ull, 0ull};  // fp32 pairs: even / odd elements
-      for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
-        uint4 xv[2][kLoadBatch], rv[2][kLoadBatch];
+    if constexpr (GRID) {
+      // Whole rows: every CTA forms h = x + r over the entire row and its sum of squares
+      // itself, chunk j of row m in thread j % 256 and in the same order in every CTA, so
+      // all CTAs of a tile group get the same rstd and none waits for another.  h of this
+      // CTA's K slice goes into the operand buffer; tile group 0 writes the updated
+      // residual of its slices.  Rows M .. 15 of the buffer are left as they are: they only
+      // reach accumulator columns that are never read.
+      const int row_chunks = p.H >> 3;  // H % 8 == 0 on this path
+      const int cpt = (row_chunks + kNormThreads - 1) / kNormThreads;  // chunks per thread and row
+      const int units = p.M * cpt;
+      const int j_lo = (int)(k_lo >> 3);
+      uint64_t ssg[kGridMaxM];
 #pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int m = m0 + kNormWarps * q2;
-          const bool live = m < p.M;
-          const uint16_t* xr = p.x + (int64_t)m * p.ldx;
-          const uint16_t* rr = p.r ? p.r + (int64_t)m * p.ldr : nullptr;
+      for (int m = 0; m < kGridMaxM; ++m) ssg[m] = 0ull;
+      for (int u0 = 0; u0 < units; u0 += kGridBatch) {
+        uint4 xv[kGridBatch], rv[kGridBatch];
 #pragma unroll
-          for (int b = 0; b < kLoadBatch; ++b) {
-            const int j = j0 + lane + 32 * b;
-            const int64_t k = k_lo + (int64_t)j * 8;
-            xv[q2][b] = make_uint4(0, 0, 0, 0);
-            rv[q2][b] = make_uint4(0, 0, 0, 0);
-            if (live && j < nchunk && k < p.H) {
-              xv[q2][b] = __ldg(reinterpret_cast<const uint4*>(xr + k));
-              if (rr) rv[q2][b] = __ldg(reinterpret_cast<const uint4*>(rr + k));
-            }
+        for (int b = 0; b < kGridBatch; ++b) {
+          const int u = u0 + b, m = u / cpt, j = et + kNormThreads * (u - m * cpt);
+          xv[b] = rv[b] = make_uint4(0, 0, 0, 0);
+          if (u < units && j < row_chunks) {
+            xv[b] = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)m * p.ldx + (int64_t)j * 8));
+            if (p.r) rv[b] = __ldg(reinterpret_cast<const uint4*>(p.r + (int64_t)m * p.ldr + (int64_t)j * 8));
           }
         }
 #pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int m = m0 + kNormWarps * q2;
-          const bool live = m < p.M;
-          // Branch-free over the batch (predicated stores only), so the chunks interleave:
-          // x and r are zero where a chunk is out of range, so h is zero and adds nothing.
+        for (int b = 0; b < kGridBatch; ++b) {
+          const int u = u0 + b, m = u / cpt, j = et + kNormThreads * (u - m * cpt);  // m: same in every thread
+          if (u >= units) break;
+          const uint4 hv = p.r ? add8_rn<T>(xv[b], rv[b]) : xv[b];
 #pragma unroll
-          for (int b = 0; b < kLoadBatch; ++b) {
-            const int j = j0 + lane + 32 * b;
-            const int64_t k = k_lo + (int64_t)j * 8;
-            const uint4 hv = p.r ? add8_rn<T>(xv[q2][b], rv[q2][b]) : xv[q2][b];
-            ss2[q2] = sumsq8_f2<T>(hv, ss2[q2]);
-            if (write_res && live && j < nchunk && k < p.H)
-              *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
-            hkeep[q2][b] = hv;
-            if (j < nchunk) *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
+          for (int mm = 0; mm < kGridMaxM; ++mm)
+            if (mm == m) ssg[mm] = sumsq8_f2<T>(hv, ssg[mm]);
+          const int js = j - j_lo;  // chunk within this CTA's slice
+          if (j < row_chunks && js >= 0 && js < nchunk) {
+            *reinterpret_cast<uint4*>(normed + (js >> 3) * (MPAD * 128) + sw128_offset(m, js & 7)) = hv;
+            if (write_res) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + (int64_t)j * 8) = hv;
           }
         }
       }
+      // The slice's chunks past the end of the row (H % 64 != 0) meet the weight map's
+      // zero fill; they must hold finite values, so zeros.
+      for (int t = et; t < p.M * nchunk; t += kNormThreads) {
+        const int m = t / nchunk, js = t - m * nchunk;
+        if (j_lo + js >= row_chunks)
+          *reinterpret_cast<uint4*>(normed + (js >> 3) * (MPAD * 128) + sw128_offset(m, js & 7)) =
+              make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        float lo, hi;
-        f2_unpack(ss2[q2], lo, hi);
-        float ss = lo + hi;
+      for (int m = 0; m < kGridMaxM; ++m) {
+        if (m < p.M) {
+          float lo, hi;
+          f2_unpack(ssg[m], lo, hi);
+          float ss = lo + hi;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) rowp[m0 + kNormWarps * q2] = ss;
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          if (lane == 0) red[nw * MPAD + m] = ss;
+        }
+      }
+    } else {
+      for (int m0 = nw; m0 < MPAD; m0 += 2 * kNormWarps) {
+        uint64_t ss2[2] = {0ull, 0ull};  // fp32 pairs: even / odd elements
+        for (int j0 = 0; j0 < nchunk; j0 += 32 * kLoadBatch) {
+          uint4 xv[2][kLoadBatch], rv[2][kLoadBatch];
+  #pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int m = m0 + kNormWarps * q2;
+            const bool live = m < p.M;
+            const uint16_t* xr = p.x + (int64_t)m * p.ldx;
+            const uint16_t* rr = p.r ? p.r + (int64_t)m * p.ldr : nullptr;
+  #pragma unroll
+            for (int b = 0; b < kLoadBatch; ++b) {
+              const int j = j0 + lane + 32 * b;
+              const int64_t k = k_lo + (int64_t)j * 8;
+              xv[q2][b] = make_uint4(0, 0, 0, 0);
+              rv[q2][b] = make_uint4(0, 0, 0, 0);
+              if (live && j < nchunk && k < p.H) {
+                xv[q2][b] = __ldg(reinterpret_cast<const uint4*>(xr + k));
+                if (rr) rv[q2][b] = __ldg(reinterpret_cast<const uint4*>(rr + k));
+              }
+            }
+          }
+  #pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int m = m0 + kNormWarps * q2;
+            const bool live = m < p.M;
+            // Branch-free over the batch (predicated stores only), so the chunks interleave:
+            // x and r are zero where a chunk is out of range, so h is zero and adds nothing.
+  #pragma unroll
+            for (int b = 0; b < kLoadBatch; ++b) {
+              const int j = j0 + lane + 32 * b;
+              const int64_t k = k_lo + (int64_t)j * 8;
+              const uint4 hv = p.r ? add8_rn<T>(xv[q2][b], rv[q2][b]) : xv[q2][b];
+              ss2[q2] = sumsq8_f2<T>(hv, ss2[q2]);
+              if (write_res && live && j < nchunk && k < p.H)
+                *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
+              hkeep[q2][b] = hv;
+              if (j < nchunk) *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
+            }
+          }
+        }
+  #pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          float lo, hi;
+          f2_unpack(ss2[q2], lo, hi);
+          float ss = lo + hi;
+  #pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          if (lane == 0) rowp[m0 + kNormWarps * q2] = ss;
+        }
       }
     }
 #pragma unroll
@@ -418,20 +484,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("bar.sync 1, 256;" ::: "memory");
     // Every activation load has returned: the producer may now fill the whole ring.
     if (et == 0) mbar_arrive(acts_bar);
-    // Publish this CTA's per-row partial sums into slot `rank` of every CTA: each st.async
-    // counts its 4 bytes on the receiving CTA's sum_bar.
-    if (warp == 2) {
-      for (uint32_t c = 0; c < C; ++c) {
-        const uint32_t bar_c = mapa_shared(smem_u32(sum_bar), c);
-        for (int m = lane; m < MPAD; m += 32)
-          st_async_f32(mapa_shared(smem_u32(&red[rank * MPAD + m]), c), rowp[m], bar_c);
+    if constexpr (GRID) {
+      // Whole-row sums: the eight warps' shares, added in warp order.
+      for (int m = et; m < p.M; m += kNormThreads) {
+        float tot = 0.f;
+        for (int w = 0; w < kNormWarps; ++w) tot += red[w * MPAD + m];
+        rstd_s[m] = row_rstd(tot, p.H, p.eps);
       }
-    }
-    ok = mbar_wait<true>(sum_bar, 0);
-    for (int m = et; m < MPAD; m += kNormThreads) {
-      float tot = 0.f;
-      for (uint32_t c = 0; c < C; ++c) tot += red[c * MPAD + m];
-      rstd_s[m] = row_rstd(tot, p.H, p.eps);
+    } else {
+      // Publish this CTA's per-row partial sums into slot `rank` of every CTA: each st.async
+      // counts its 4 bytes on the receiving CTA's sum_bar.
+      if (warp == 2) {
+        for (uint32_t c = 0; c < C; ++c) {
+          const uint32_t bar_c = mapa_shared(smem_u32(sum_bar), c);
+          for (int m = lane; m < MPAD; m += 32)
+            st_async_f32(mapa_shared(smem_u32(&red[rank * MPAD + m]), c), rowp[m], bar_c);
+        }
+      }
+      ok = mbar_wait<true>(sum_bar, 0);
+      for (int m = et; m < MPAD; m += kNormThreads) {
+        float tot = 0.f;
+        for (uint32_t c = 0; c < C; ++c) tot += red[c * MPAD + m];
+        rstd_s[m] = row_rstd(tot, p.H, p.eps);
+      }
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
     // Pass 2: normalise, dtype((h * rstd) * g), over pass 1's rows and chunks; a lane's gain
@@ -526,63 +601,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = bar_and(1, kNormThreads, wok) && ok;  // every warp has left the loop
     }
 
-    // Epilogue: TMEM -> registers -> this CTA's partial tile in shared memory, laid out
-    // [m][nt][row] so that every rank's share is one contiguous byte range.
     ok = mbar_wait(accum_bar, 0) && ok;
     tc_fence_after();
     const int q = warp & 3;             // TMEM lane quadrant this warp may access
     const int half = (warp - 2) >> 2;   // the two warps of a quadrant split the 16-column chunks
     const int row = q * 32 + lane;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-      for (int c0 = 0; c0 < MPAD; c0 += 16) {
-        if (((nt * (MPAD / 16) + c0 / 16) & 1) != half) continue;
-        uint32_t v[16];
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + nt * MPAD + c0, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) part[((c0 + e) * NT + nt) * kTileRows + row] = __uint_as_float(v[e]);
-      }
-    }
-    tc_fence_before();
-    // The bulk copies read the partial tile through the async proxy.
-    fence_proxy_async_smem();
-    // One release per CTA: the CTA barrier orders every thread's partial-tile writes before
-    // thread 0's cluster fence, which the relaxed remote arrives then publish.  An arrival
-    // also says that this CTA's MMAs have retired, so its ring may receive the peers' slices.
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (et == 0) {
-      fence_acq_rel_cluster();
-      for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
-    }
-    ok = mbar_wait<true>(part_bar, 0) && ok;
-    // Lane c of warp 2 sends rank c's share of this CTA's partial tile to slot `rank` of
-    // rank c's ring.
-    if (warp == 2 && (uint32_t)lane < C && (uint32_t)lane != rank) {
-      const uint32_t o = (uint32_t)lane, f0 = share(o), nb = 16u * (share(o + 1) - f0);
-      if (nb > 0)
-        bulk_copy_to_peer(mapa_shared(smem_u32(recv) + rank * slot_bytes, o), smem_u32(part) + 16u * f0, nb,
-                          mapa_shared(smem_u32(recv_bar), o));
-    }
-    ok = mbar_wait<true>(recv_bar, 0) && ok;
-    // Every copy into this CTA has landed, so their sources have been read: this thread
-    // makes no further access to a peer's shared memory, nor a peer to this CTA's.
-    cluster_arrive_release_thread();
-    // Reduce this CTA's share: the C partials of each quad in rank order (deterministic).
-    const uint32_t f0 = share(rank), f1 = share(rank + 1);
-    const float4* part4 = reinterpret_cast<const float4*>(part);
-    const float4* recv4 = reinterpret_cast<const float4*>(recv);
+    // Quad f = ((m * NT + nt) * 128 + row) / 4 of the k-summed tile: four output features
+    // of token m, rounded to the dtype and stored.
     const bool vec_store = (p.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 7) == 0;
-    for (uint32_t f = f0 + et; f < f1; f += kNormThreads) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t c = 0; c < C; ++c) {
-        const float4 v = c == rank ? part4[f] : recv4[c * (slot_bytes / 16) + (f - f0)];
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
+    auto store_quad = [&](uint32_t f, float4 acc) {
       const int nl = (int)(f % (kTileRows / 4)) * 4;
       const uint32_t mn = f / (kTileRows / 4);
       const int nt = (int)(mn % NT), m = (int)(mn / NT);
@@ -601,6 +628,104 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           if (n + e < p.N) dst[e] = Elem<T>::from_f(a4[e]);
+      }
+    };
+    if constexpr (GRID) {
+      // Grid epilogue: this CTA's partial tile [m][nt][row] (tokens m < M) goes to its slot
+      // in the workspace; the CTA that arrives last on the tile group's counter sums the C
+      // slots in rank order (the result does not depend on arrival order), stores the tile
+      // and puts the counter back to zero.  Nobody waits for another CTA.  A CTA whose
+      // bounded waits gave up still arrives, so the counter stays consistent.
+      const uint32_t grp = blockIdx.y;
+      const int slot_floats = p.M * NT * kTileRows;
+      float* slot = p.gpart + ((int64_t)grp * C + rank) * slot_floats;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if ((nt & 1) != half) continue;
+        uint32_t v[16];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + nt * MPAD, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (e < p.M) slot[(e * NT + nt) * kTileRows + row] = __uint_as_float(v[e]);
+      }
+      tc_fence_before();
+      __threadfence();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      volatile uint32_t* last_flag = tmem_slot + 1;
+      if (et == 0) *last_flag = atomicAdd(p.gcnt + grp, 1) == (int)C - 1 ? 1u : 0u;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (*last_flag) {
+        __threadfence();
+        const float4* slots4 = reinterpret_cast<const float4*>(p.gpart + (int64_t)grp * C * slot_floats);
+        const uint32_t total4 = (uint32_t)(slot_floats / 4);
+        for (uint32_t f = et; f < total4; f += kNormThreads) {
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (uint32_t c = 0; c < C; ++c) {
+            const float4 v = __ldcg(slots4 + c * total4 + f);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+          }
+          store_quad(f, acc);
+        }
+        if (et == 0) p.gcnt[grp] = 0;
+      }
+      cluster_arrive_release_thread();  // the teardown's (one-CTA) cluster barrier
+    } else {
+      // Cluster epilogue: TMEM -> registers -> this CTA's partial tile in shared memory, laid
+      // out [m][nt][row] so that every rank's share is one contiguous byte range.
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int c0 = 0; c0 < MPAD; c0 += 16) {
+          if (((nt * (MPAD / 16) + c0 / 16) & 1) != half) continue;
+          uint32_t v[16];
+          tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + nt * MPAD + c0, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) part[((c0 + e) * NT + nt) * kTileRows + row] = __uint_as_float(v[e]);
+        }
+      }
+      tc_fence_before();
+      // The bulk copies read the partial tile through the async proxy.
+      fence_proxy_async_smem();
+      // One release per CTA: the CTA barrier orders every thread's partial-tile writes before
+      // thread 0's cluster fence, which the relaxed remote arrives then publish.  An arrival
+      // also says that this CTA's MMAs have retired, so its ring may receive the peers' slices.
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (et == 0) {
+        fence_acq_rel_cluster();
+        for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
+      }
+      ok = mbar_wait<true>(part_bar, 0) && ok;
+      // Lane c of warp 2 sends rank c's share of this CTA's partial tile to slot `rank` of
+      // rank c's ring.
+      if (warp == 2 && (uint32_t)lane < C && (uint32_t)lane != rank) {
+        const uint32_t o = (uint32_t)lane, f0 = share(o), nb = 16u * (share(o + 1) - f0);
+        if (nb > 0)
+          bulk_copy_to_peer(mapa_shared(smem_u32(recv) + rank * slot_bytes, o), smem_u32(part) + 16u * f0, nb,
+                            mapa_shared(smem_u32(recv_bar), o));
+      }
+      ok = mbar_wait<true>(recv_bar, 0) && ok;
+      // Every copy into this CTA has landed, so their sources have been read: this thread
+      // makes no further access to a peer's shared memory, nor a peer to this CTA's.
+      cluster_arrive_release_thread();
+      // Reduce this CTA's share: the C partials of each quad in rank order (deterministic).
+      const uint32_t f0 = share(rank), f1 = share(rank + 1);
+      const float4* part4 = reinterpret_cast<const float4*>(part);
+      const float4* recv4 = reinterpret_cast<const float4*>(recv);
+      for (uint32_t f = f0 + et; f < f1; f += kNormThreads) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t c = 0; c < C; ++c) {
+          const float4 v = c == rank ? part4[f] : recv4[c * (slot_bytes / 16) + (f - f0)];
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        store_quad(f, acc);
       }
     }
     (void)ok;
@@ -621,9 +746,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int MPAD, int NT, bool F8>
+template <int MPAD, int NT, bool F8, bool GRID = false>
 auto kernel_ptr(bool bf16) {
-  return bf16 ? decode_kernel<__nv_bfloat16, MPAD, NT, F8> : decode_kernel<__half, MPAD, NT, F8>;
+  return bf16 ? decode_kernel<__nv_bfloat16, MPAD, NT, F8, GRID> : decode_kernel<__half, MPAD, NT, F8, GRID>;
 }
 
 using KernelFn = void (*)(CUtensorMap, DecodeParams, int);
@@ -650,13 +775,25 @@ KernelFn pick_kernel(int mpad, int nt, bool bf16, bool f8) {
   return f8 ? pick_kernel_t<true>(mpad, nt, bf16) : pick_kernel_t<false>(mpad, nt, bf16);
 }
 
+// Grid variant: 16-bit weights, MPAD 16, 1 to 5 tiles per CTA.
+KernelFn pick_grid_kernel(int nt, bool bf16) {
+  switch (nt) {
+    case 1: return kernel_ptr<16, 1, false, true>(bf16);
+    case 2: return kernel_ptr<16, 2, false, true>(bf16);
+    case 3: return kernel_ptr<16, 3, false, true>(bf16);
+    case 4: return kernel_ptr<16, 4, false, true>(bf16);
+    case 5: return kernel_ptr<16, 5, false, true>(bf16);
+    default: return nullptr;
+  }
+}
+
 cudaLaunchConfig_t base_config(const DecodeConfig& c, int tiles, cudaLaunchAttribute* attr, int* na) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)c.cluster, (unsigned)tiles);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = c.smem;
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)c.cluster;
+  attr[0].val.clusterDim.x = c.grid ? 1u : (unsigned)c.cluster;  // grid variant: K split without a cluster
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   *na = 1;
@@ -774,9 +911,57 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, boo
   return rc;
 }
 
+// The counters take a fixed region whatever the shape, so that one zero-filled workspace
+// serves launches of different shapes: another shape's partial slots never overlap them.
+int64_t decode_grid_counter_bytes() { return (int64_t)kGridMaxTiles * 4; }
+
+// Counters, then the partial slots: groups x S x M x NT x 128 fp32, bounded by
+// S <= kGridMaxSplit and groups x NT x 128 <= (ceil(N / 128) + kMaxNT) x 128.
+int64_t decode_grid_workspace_bytes(int64_t M, int64_t N) {
+  const int64_t tiles = (N + kTileRows - 1) / kTileRows;
+  return decode_grid_counter_bytes() + (int64_t)kGridMaxSplit * (tiles + kMaxNT) * kTileRows * M * 4;
+}
+
+// Grid variant: NT tiles per CTA, S = cluster CTAs per tile group splitting K, S x groups
+// <= SM count (one wave at one CTA per SM), S <= kGridMaxSplit.  The configuration with the
+// fewest weight k-blocks per CTA wins (ties: more CTAs, then the deeper ring).
+// FQKV_DECODE_NT / FQKV_DECODE_STAGES restrict the search as for the cluster kernel.
+int decode_grid_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg) {
+  if (M < 1 || M > kGridMaxM || (N + kTileRows - 1) / kTileRows > kGridMaxTiles) return FQKV_ERR_SCHEDULE;
+  static const int force_nt = env_int("FQKV_DECODE_NT", 0);
+  static const int force_s = env_int("FQKV_DECODE_STAGES", 0);
+  const int KB = (H + kKBlock - 1) / kKBlock;
+  DecodeConfig best{};
+  long best_cost = -1, best_ctas = 0;
+  for (int nt = 1; nt <= kMaxNT; ++nt) {
+    if (force_nt && nt != force_nt) continue;
+    const int groups = (N + nt * kTileRows - 1) / (nt * kTileRows);
+    if (groups > sm_count) continue;
+    const int S = std::min(std::min(sm_count / groups, kGridMaxSplit), KB);
+    const int nkb_max = (KB + S - 1) / S;
+    if (nkb_max * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
+    const long cost = (long)nt * nkb_max, ctas = (long)groups * S;
+    for (int st = 16; st >= 2; --st) {
+      if (force_s && st != force_s) continue;
+      DecodeConfig t{16, nt, st, S, 0, 0, 0, 1};
+      t.smem = decode_smem_bytes(t, KB);
+      if (t.smem > kSmemLimit) continue;
+      if (best_cost < 0 || cost < best_cost || (cost == best_cost && ctas > best_ctas)) {
+        best_cost = cost;
+        best_ctas = ctas;
+        best = t;
+      }
+      break;  // deepest ring that fits for this NT
+    }
+  }
+  if (best_cost < 0) return FQKV_ERR_SCHEDULE;
+  *cfg = best;
+  return 0;
+}
+
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream) {
-  KernelFn k = pick_kernel(c.mpad, c.nt, bf16, c.f8 != 0);
+  KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16) : pick_kernel(c.mpad, c.nt, bf16, c.f8 != 0);
   if (!k) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(k), c.smem);
   if (e != cudaSuccess) return e;
@@ -792,8 +977,13 @@ cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const D
   }
   cfg.numAttrs = na;
   DecodeParams q = p;
-  static const int pre_stages = env_int("FQKV_DECODE_PRE", 2);  // read once per process
-  q.pre_stages = pre_stages;
+  // Weight stages issued before the activation loads: 2 for the cluster kernel (swept 0-6
+  // at NT = 2 on B200); about 64 KB for the grid variant, whose whole-row activation phase
+  // is longer (graph-timed, Qwen2-7B shape, M = 1, NT = 1: 11.80 / 11.37 / 11.25 us with 2 /
+  // 3 / 4 stages of 16 KB; at NT = 2, 2 stages beat 1).
+  static const int pre_env = env_int("FQKV_DECODE_PRE", 0);  // read once per process
+  const int grid_pre = std::max(1, (64 << 10) / (c.nt * kWTileBytes));
+  q.pre_stages = pre_env > 0 ? pre_env : c.grid ? grid_pre : 2;
   q.recv_in_normed = c.recv_in_normed;
   return cudaLaunchKernelEx(&cfg, k, tmW, q, c.stages);
 }

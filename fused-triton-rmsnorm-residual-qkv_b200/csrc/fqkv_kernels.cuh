@@ -67,6 +67,10 @@ struct DecodeParams {
   int recv_in_normed; // the epilogue's receive slots use the (then idle) normalised-activation
                       // buffer instead of the ring
   const float* wscale;  // e4m3 weights: fp32 scale per weight row (output feature); else null
+  // Grid variant (no cluster): per-CTA partial slots [groups][S][M][NT * 128] fp32 and one
+  // arrival counter per tile group (zero on entry, left zero on exit).
+  float* gpart;
+  int* gcnt;
 };
 
 struct StreamKParams {
@@ -325,9 +329,20 @@ struct DecodeConfig {
   size_t smem;  // dynamic shared memory bytes
   int recv_in_normed;  // see DecodeParams
   int f8;       // e4m3 weights (converted to the dtype in shared memory before the MMA)
+  int grid;     // 1: `cluster` independent CTAs split K (no cluster); they sum their partial
+                // tiles through the workspace
 };
 
 int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, bool f8 = false);
+// Grid variant of the fused decode kernel: every CTA reads whole activation rows, so it
+// serves few rows only.
+constexpr int kGridMaxM = 8;
+constexpr int kGridMaxSplit = 8;  // CTAs splitting K per tile group
+constexpr int kGridMaxTiles = 1024;  // 128-row tiles (N <= 131072): counters in the workspace
+int decode_grid_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg);
+// Workspace of the grid variant: [kGridMaxTiles arrival counters][partial slots].
+int64_t decode_grid_counter_bytes();
+int64_t decode_grid_workspace_bytes(int64_t M, int64_t N);
 // 128-row weight tiles per TMA box of the decode kernel's weight map: one box per stage
 // for NT <= 2, else NT boxes of 128 rows (a box dimension is at most 256 elements).
 __host__ __device__ constexpr int decode_box_tiles(int nt) { return nt <= 2 ? nt : 1; }

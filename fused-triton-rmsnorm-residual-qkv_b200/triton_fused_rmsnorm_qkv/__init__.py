@@ -4,7 +4,8 @@ Import-compatible with the reference package ``triton_fused_rmsnorm_qkv``
 (``src/triton_fused_rmsnorm_qkv/__init__.py:1-17``): the same six names, plus
 ``fused_add_rmsnorm_matmul`` (returns the updated residual as well) and
 ``qkv_rope_split`` (head-major Q/K/V with the rotary embedding, one launch) and
-``fused_add_rmsnorm_matmul_fp8w`` (e4m3 weights with a scale per row, decode sizes).  The GPU entry
+``fused_add_rmsnorm_matmul_fp8w`` (e4m3 weights with a scale per row, decode sizes) and
+``schedule_info`` (the schedule an automatic call of a shape runs).  The GPU entry
 points run sm_100a CUDA kernels from ``libfqkv.so``; they raise if that library is
 missing instead of falling back to anything else.
 """
@@ -20,6 +21,7 @@ from .kernel import (
     get_autotune_best_config,
     qkv_rope_split,
     quantize_weight_e4m3,
+    schedule_info,
 )
 
 __all__ = [
@@ -34,4 +36,5 @@ __all__ = [
     "qkv_rope_split",
     "fused_add_rmsnorm_matmul_fp8w",
     "quantize_weight_e4m3",
+    "schedule_info",
 ]

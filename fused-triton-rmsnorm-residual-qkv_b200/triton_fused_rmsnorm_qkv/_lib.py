@@ -16,13 +16,14 @@ from pathlib import Path
 
 # Constants mirrored from include/fused_rmsnorm_qkv.h.
 F16, BF16, F32 = 0, 1, 2
-SCHED_AUTO, SCHED_SIMT, SCHED_DECODE, SCHED_SPLIT, SCHED_PREFILL = -1, 0, 1, 2, 3
+SCHED_AUTO, SCHED_SIMT, SCHED_DECODE, SCHED_SPLIT, SCHED_PREFILL, SCHED_GRID = -1, 0, 1, 2, 3, 4
 FLAG_PDL, FLAG_STATIC_WEIGHTS = 1, 2
 ERR_NULL, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_WORKSPACE, ERR_SCHEDULE, ERR_DEVICE, ERR_DEVICE_TIMEOUT, ERR_ALIAS = (
     1, 2, 3, 4, 5, 6, 7, 8, 9)
 STATUS_WAIT_TIMEOUT = 1
 
-SCHEDULE_NAMES = {SCHED_SIMT: "simt", SCHED_DECODE: "decode", SCHED_SPLIT: "split", SCHED_PREFILL: "prefill"}
+SCHEDULE_NAMES = {SCHED_SIMT: "simt", SCHED_DECODE: "decode", SCHED_SPLIT: "split", SCHED_PREFILL: "prefill",
+                  SCHED_GRID: "grid"}
 SCHEDULE_BY_NAME = {v: k for k, v in SCHEDULE_NAMES.items()}
 SCHEDULE_BY_NAME["auto"] = SCHED_AUTO
 SCHEDULE_BY_NAME["naive"] = SCHED_SIMT

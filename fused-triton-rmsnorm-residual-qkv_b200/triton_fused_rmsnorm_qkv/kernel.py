@@ -15,6 +15,11 @@ library chooses one of its kernel families from (M, H, N, SM count):
 * ``decode``  (M <= 64): one fused kernel -- swap-AB tcgen05 MMA, the weight streamed
   by TMA, K split across a thread-block cluster whose CTAs exchange row sums of
   squares and partial tiles through distributed shared memory.
+* ``grid``    (M <= 8): the same fused kernel without clusters, so that its CTAs cover
+  nearly every SM.  Each CTA reads the whole activation rows, and the CTA that finishes a
+  tile last sums the partial tiles through a zero-filled workspace this module keeps per
+  device and stream.  Chosen automatically for M <= ``_GRID_AUTO_MAX_M`` when it cuts the
+  weight bytes per CTA well below the cluster kernel's (``_grid_preferred``).
 * ``split``   (M <= 64 when no decode configuration fits the device, or when forced; up
   to M = 128): norm pre-pass + a stream-K swap-AB GEMM reading the normalised rows by TMA.
 * ``prefill`` (M > 64): norm pre-pass + persistent 128 x BN tcgen05 GEMM.
@@ -48,6 +53,21 @@ _seen_shapes: dict[tuple[int, int], int] = {}
 # Workspace bytes per (M, H, N, dtype, schedule, device): the library's answer depends only
 # on these, and asking it every call costs a round trip through ctypes.
 _ws_bytes: dict[tuple, int] = {}
+
+# The automatic choice of the grid schedule: at most this many rows (every CTA reads whole
+# rows, which stops paying beyond a few), and at most this fraction of the cluster kernel's
+# weight bytes per CTA.  Measured on B200, graph-timed, M = 1 (cluster -> grid, us):
+# Qwen2-7B 12.70 -> 11.25 (fraction 0.74); Llama-3-8B 12.04 -> 14.0 (0.85); Llama-3-70B
+# 32.8 -> 33.9 (0.88); the gate/up weight 42.9 -> 42.6 (1.0, the same configuration).  At
+# M = 4 the Qwen2-7B shape is 12.9 against 13.2 us.
+_GRID_AUTO_MAX_M = 2
+_GRID_AUTO_MAX_BYTES = 0.8
+# (M, H, N, dtype, device) -> whether the automatic choice is the grid schedule.
+_grid_choice: dict[tuple, bool] = {}
+# (device, stream) -> zero-filled workspace of the grid schedule.  Its launches leave the
+# arrival counters at zero, and launches on one stream run in order, so one buffer per
+# stream is zeroed once and then reused.
+_grid_ws: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _env_flag(name: str) -> bool:
@@ -89,6 +109,48 @@ def _row_stride(t: torch.Tensor) -> int:
     return t.stride(-2) if t.dim() >= 2 else t.shape[-1]
 
 
+def _kblocks_per_cta(info: dict, H: int) -> int:
+    """Weight k-blocks (128 rows x 64) one CTA of a decode configuration streams."""
+    kb = (H + 63) // 64
+    return info["block_n"] // 128 * -(-kb // info["split_k"])
+
+
+def _grid_preferred(M: int, H: int, N: int, dtype_code: int, index: int) -> bool:
+    """Whether the automatic schedule for this shape is ``grid``: at most
+    ``_GRID_AUTO_MAX_M`` rows, the library would pick the cluster decode kernel, and the
+    grid configuration streams at most ``_GRID_AUTO_MAX_BYTES`` of its weight bytes per CTA."""
+    key = (M, H, N, dtype_code, index)
+    hit = _grid_choice.get(key)
+    if hit is None:
+        hit = False
+        if M <= _GRID_AUTO_MAX_M:
+            auto = _lib.query_schedule(M, H, N, dtype_code, _lib.SCHED_AUTO)
+            if auto["schedule"] == _lib.SCHED_DECODE:
+                try:
+                    grid = _lib.query_schedule(M, H, N, dtype_code, _lib.SCHED_GRID)
+                except (RuntimeError, ValueError, TypeError):
+                    grid = None
+                hit = grid is not None and (
+                    _kblocks_per_cta(grid, H) <= _GRID_AUTO_MAX_BYTES * _kblocks_per_cta(auto, H))
+        _grid_choice[key] = hit
+    return hit
+
+
+def _tma_ready(H: int, tensors, strides) -> bool:
+    """The alignment the library's tensor-core schedules need (else it runs ``simt``)."""
+    return (H % 8 == 0 and H <= 16384 and all(t.data_ptr() % 16 == 0 for t in tensors)
+            and all(s % 8 == 0 for s in strides))
+
+
+def _grid_workspace(index: int, stream: int, nbytes: int, dev: torch.device) -> torch.Tensor:
+    """The zero-filled grid-schedule workspace of this device and stream, grown as needed."""
+    buf = _grid_ws.get((index, stream))
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _grid_ws[(index, stream)] = buf
+    return buf
+
+
 def _launch(x2: torch.Tensor, r2: Optional[torch.Tensor], rms_weight: torch.Tensor, weight: torch.Tensor,
             out2: torch.Tensor, rout2: Optional[torch.Tensor], eps: float, schedule: int,
             static_weights: bool, M: int) -> None:
@@ -121,12 +183,21 @@ def _launch(x2: torch.Tensor, r2: Optional[torch.Tensor], rms_weight: torch.Tens
         flags |= _lib.FLAG_STATIC_WEIGHTS
     ctx = contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
     with ctx:
+        dt = _DTYPE_CODE[x2.dtype]
+        if code == _lib.SCHED_AUTO and M <= _GRID_AUTO_MAX_M and _grid_preferred(M, H, N, dt, dev.index):
+            tensors = [t for t in (x2, r2, g, w, rout2) if t is not None]
+            strides = [_row_stride(x2), w.stride(0)] + [_row_stride(t) for t in (r2, rout2) if t is not None]
+            if _tma_ready(H, tensors, strides):
+                code = _lib.SCHED_GRID
         key = (M, H, N, x2.dtype, code, dev.index)
         ws_bytes = _ws_bytes.get(key)
         if ws_bytes is None:
-            ws_bytes = _ws_bytes[key] = _lib.workspace_bytes(M, H, N, _DTYPE_CODE[x2.dtype], code)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+            ws_bytes = _ws_bytes[key] = _lib.workspace_bytes(M, H, N, dt, code)
         stream = _current_stream(dev.index)
+        if code == _lib.SCHED_GRID:
+            ws = _grid_workspace(dev.index, stream, ws_bytes, dev)
+        else:
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
         rc = _lib.launch(
             x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), _GAIN_CODE[g.dtype],
             w.data_ptr(), out2.data_ptr(), rout2.data_ptr() if rout2 is not None else None,
@@ -183,7 +254,7 @@ def fused_rmsnorm_residual_matmul(
         weight: (N_OUT, H) projection, e.g. the packed GQA weight [Wq; Wk; Wv].
         eps: RMSNorm epsilon.
         residual_out: optional (B, S, H) tensor that receives x + residual.
-        schedule: None/"auto", "decode", "split", "prefill" or "simt" ("naive").
+        schedule: None/"auto", "decode", "grid", "split", "prefill" or "simt" ("naive").
         static_weights: weight is not written by the preceding kernel in the stream
             (default: environment variable FQKV_STATIC_WEIGHTS).
 
@@ -406,6 +477,15 @@ def fused_rmsnorm_residual_qkv_fixed(
     return q, k, v
 
 
+def schedule_info(M: int, H: int, N: int, dtype: torch.dtype = torch.bfloat16) -> dict:
+    """The library's record (``fqkv_query_schedule``) of the schedule an automatically
+    scheduled call of this shape runs on the current device, with 16-byte-aligned tensors:
+    the C library's choice, or ``grid`` where this module picks it."""
+    dt = _DTYPE_CODE[dtype]
+    grid = _grid_preferred(M, H, N, dt, torch.cuda.current_device())
+    return _lib.query_schedule(M, H, N, dt, _lib.SCHED_GRID if grid else _lib.SCHED_AUTO)
+
+
 def get_autotune_best_config(M: int, H: int) -> dict | None:
     """Describe the schedule chosen for a (M, H) seen before, else None (kernel.py:558-572).
 
@@ -416,7 +496,7 @@ def get_autotune_best_config(M: int, H: int) -> dict | None:
     N = _seen_shapes.get((M, H))
     if N is None or not torch.cuda.is_available():
         return None
-    info = _lib.query_schedule(M, H, N, _lib.BF16)
+    info = schedule_info(M, H, N)
     return {
         "BLOCK_M": info["block_m"],
         "BLOCK_N": info["block_n"],

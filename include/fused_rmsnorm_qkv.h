@@ -56,6 +56,16 @@ extern "C" {
 #define FQKV_SCHED_DECODE    1  /* one fused tcgen05 kernel: swap-AB, K split across a cluster */
 #define FQKV_SCHED_SPLIT     2  /* norm pre-pass + swap-AB tcgen05 GEMM (mid-size M) */
 #define FQKV_SCHED_PREFILL   3  /* norm pre-pass + tiled tcgen05 GEMM (large M) */
+#define FQKV_SCHED_GRID      4  /* the fused decode kernel on (nearly) every SM, M <= 8 and
+                                   N <= 131072: K split over independent CTAs that each read
+                                   whole activation rows; the partial tiles are summed through
+                                   the workspace by the CTA that arrives last on a per-tile
+                                   counter (its first 4096 bytes).  Those counters must be zero
+                                   before the first launch; every completed launch leaves them
+                                   zero, whatever the shape, so a workspace kept for this
+                                   schedule on one stream is zero-filled once.  Launches that
+                                   share a workspace must not overlap on the GPU.  AUTO never
+                                   picks it. */
 
 /* Launch flags. */
 #define FQKV_FLAG_PDL            1  /* launch with programmatic dependent launch; kernels
@@ -190,7 +200,7 @@ FQKV_API int fqkv_rope_split(const void* qkv, int64_t ldq, const void* cos, cons
                 int64_t cos_batch, void* q, void* k, void* v, int64_t B, int64_t S,
                 int n_q_heads, int n_kv_heads, int head_dim, int dtype, void* stream);
 
-/* ABI version (major * 100 + minor). */
+/* ABI version (major * 100 + minor): 102 adds FQKV_SCHED_GRID. */
 FQKV_API int fqkv_version(void);
 
 #ifdef __cplusplus

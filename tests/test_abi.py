@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert _lib.version() == 101
+    assert _lib.version() == 102
 
 
 FAKE = 0x100000  # 16-byte aligned, never dereferenced: validation fails before any launch
@@ -71,6 +71,12 @@ SPACED = dict(x=1 << 32, r=2 << 32, g=3 << 32, w=4 << 32, out=5 << 32)
     (dict(flags=64), _lib.ERR_SCHEDULE),
     (dict(schedule=_lib.SCHED_DECODE, M=65), _lib.ERR_SCHEDULE),
     (dict(schedule=_lib.SCHED_SPLIT, M=129), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_GRID, M=9), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_GRID, M=1, N=131200, ldo=131200), _lib.ERR_SCHEDULE),
+    (dict(schedule=5), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_GRID, M=1, ws=None), _lib.ERR_WORKSPACE),
+    (dict(schedule=_lib.SCHED_GRID, M=1, ws=(6 << 32) + 16, ws_bytes=1 << 30), _lib.ERR_ALIGN),
+    (dict(schedule=_lib.SCHED_GRID, M=1, x=(1 << 32) + 2), _lib.ERR_ALIGN),
     (dict(schedule=_lib.SCHED_DECODE, H=260, ldx=260, ldr=260, ldw=260, ldro=260), _lib.ERR_ALIGN),
     (dict(schedule=_lib.SCHED_DECODE, x=(1 << 32) + 2), _lib.ERR_ALIGN),
     (dict(schedule=_lib.SCHED_PREFILL, M=4096, ws=None), _lib.ERR_WORKSPACE),
@@ -110,6 +116,9 @@ def _split_bytes(M, H, N):
     (16, 4096, _lib.SCHED_SPLIT, _split_bytes(16, 4096, 6144)),
     (2048, 4096, _lib.SCHED_PREFILL, 2048 * 4096 * 2),           # pre-pass scratch only
     (7, 4100, _lib.SCHED_AUTO, 0),                  # H % 8 != 0 -> SIMT, no scratch
+    # grid decode: 4096 bytes of counters + up to 8 partial slots per (48 + 5) tiles x M rows
+    (1, 4096, _lib.SCHED_GRID, 4096 + 8 * 53 * 128 * 1 * 4),
+    (8, 4096, _lib.SCHED_GRID, 4096 + 8 * 53 * 128 * 8 * 4),
     (3, 100, _lib.SCHED_SIMT, 0),
 ])
 def test_workspace_sizes(M, H, sched, expect):
