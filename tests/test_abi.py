@@ -184,3 +184,13 @@ def fp8_call(**kw):
 ])
 def test_fp8w_rejects_before_any_cuda_call(kw, code):
     assert fp8_call(**kw) == code, _lib.last_error()
+
+
+def test_profile_case_parses_its_arguments():
+    """The profiler workload module takes its shape and schedule from the command line
+    (no GPU needed to print its usage)."""
+    from triton_fused_rmsnorm_qkv import profile_case
+
+    with pytest.raises(SystemExit) as e:
+        profile_case.main(["--help"])
+    assert e.value.code == 0
