@@ -6,8 +6,9 @@ the partial tiles in rank order through a zero-filled workspace.  Checked agains
 CPU oracle (restated baseline.py) with the benchmark bars -- Q/K/V max-abs error <= 2e-2
 (1 ulp of the reference above |x| = 4 for bf16) and relative L2 error <= 5e-3, the
 updated residual bit-exact -- and for what is particular to it: repeated launches give
-identical bits and leave the arrival counters at zero, the automatic choice at M = 1 on
-the Llama-3-8B shape, ragged K and N, row-strided inputs.
+identical bits and leave the arrival counters at zero, the automatic choice (taken at M = 1
+for the Qwen2-7B shape, not for Llama-3-8B or above two rows), ragged K and N, row-strided
+inputs.
 """
 from __future__ import annotations
 
