@@ -156,56 +156,67 @@ def _launch(x2: torch.Tensor, r2: Optional[torch.Tensor], rms_weight: torch.Tens
             static_weights: bool, M: int) -> None:
     """Validate tensor metadata and call ``fqkv_launch`` on the current stream.  The
     activation, output and residual-out tensors are M rows of H (N) elements with one row
-    stride each (see ``_rows``)."""
+    stride each (see ``_rows``).  Every call goes through here, so it reads each piece of
+    metadata once."""
     H = x2.shape[-1]
     N = weight.shape[0]
-    if x2.dtype not in _DTYPE_CODE:
-        raise TypeError(f"x must be float16 or bfloat16, got {x2.dtype}")
-    if weight.dtype != x2.dtype:
-        raise TypeError(f"weight dtype {weight.dtype} does not match x dtype {x2.dtype}")
-    if r2 is not None and r2.dtype != x2.dtype:
-        raise TypeError(f"residual dtype {r2.dtype} does not match x dtype {x2.dtype}")
-    if rms_weight.dtype not in _GAIN_CODE:
+    xdt = x2.dtype
+    dt = _DTYPE_CODE.get(xdt)
+    if dt is None:
+        raise TypeError(f"x must be float16 or bfloat16, got {xdt}")
+    if weight.dtype != xdt:
+        raise TypeError(f"weight dtype {weight.dtype} does not match x dtype {xdt}")
+    if r2 is not None and r2.dtype != xdt:
+        raise TypeError(f"residual dtype {r2.dtype} does not match x dtype {xdt}")
+    gcode = _GAIN_CODE.get(rms_weight.dtype)
+    if gcode is None:
         raise TypeError(f"rms_weight must be float32, float16 or bfloat16, got {rms_weight.dtype}")
     if rms_weight.numel() != H:
         raise ValueError(f"rms_weight must have H={H} elements, got shape {tuple(rms_weight.shape)}")
-    dev = x2.device
+    index = x2.get_device()
     for name, t in (("residual", r2), ("rms_weight", rms_weight), ("weight", weight)):
-        if t is not None and t.device != dev:
-            raise ValueError(f"{name} is on {t.device}, x is on {dev}")
-    g = rms_weight.reshape(H)
+        if t is not None and t.get_device() != index:
+            raise ValueError(f"{name} is on {t.device}, x is on {x2.device}")
+    g = rms_weight if rms_weight.dim() == 1 else rms_weight.reshape(H)
     if g.stride(0) != 1:
         g = g.contiguous()
     w = weight if weight.stride(1) == 1 else weight.contiguous()
     code = _schedule_code(schedule)
-    flags = _lib.FLAG_PDL
-    if static_weights:
-        flags |= _lib.FLAG_STATIC_WEIGHTS
-    ctx = contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
-    with ctx:
-        dt = _DTYPE_CODE[x2.dtype]
-        if code == _lib.SCHED_AUTO and M <= _GRID_AUTO_MAX_M and _grid_preferred(M, H, N, dt, dev.index):
-            tensors = [t for t in (x2, r2, g, w, rout2) if t is not None]
-            strides = [_row_stride(x2), w.stride(0)] + [_row_stride(t) for t in (r2, rout2) if t is not None]
-            if _tma_ready(H, tensors, strides):
-                code = _lib.SCHED_GRID
-        key = (M, H, N, x2.dtype, code, dev.index)
-        ws_bytes = _ws_bytes.get(key)
-        if ws_bytes is None:
-            ws_bytes = _ws_bytes[key] = _lib.workspace_bytes(M, H, N, dt, code)
-        stream = _current_stream(dev.index)
-        if code == _lib.SCHED_GRID:
-            ws = _grid_workspace(dev.index, stream, ws_bytes, dev)
-        else:
-            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
-        rc = _lib.launch(
-            x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), _GAIN_CODE[g.dtype],
-            w.data_ptr(), out2.data_ptr(), rout2.data_ptr() if rout2 is not None else None,
-            M, H, N, _row_stride(x2), _row_stride(r2) if r2 is not None else 0, w.stride(0), _row_stride(out2),
-            _row_stride(rout2) if rout2 is not None else 0, float(eps), _DTYPE_CODE[x2.dtype], code, flags,
-            ws.data_ptr() if ws is not None else None, ws_bytes, stream)
+    flags = _lib.FLAG_PDL | (_lib.FLAG_STATIC_WEIGHTS if static_weights else 0)
+    ldx, ldw, ldo = _row_stride(x2), w.stride(0), _row_stride(out2)
+    ldr = _row_stride(r2) if r2 is not None else 0
+    ldro = _row_stride(rout2) if rout2 is not None else 0
+    if index == torch.cuda.current_device():
+        rc = _call(x2, r2, g, gcode, w, out2, rout2, M, H, N, ldx, ldr, ldw, ldo, ldro, eps, dt, code, flags, index)
+    else:
+        with torch.cuda.device(index):
+            rc = _call(x2, r2, g, gcode, w, out2, rout2, M, H, N, ldx, ldr, ldw, ldo, ldro, eps, dt, code, flags,
+                       index)
     _lib.check(rc)
     _seen_shapes[(M, H)] = N
+
+
+def _call(x2, r2, g, gcode, w, out2, rout2, M, H, N, ldx, ldr, ldw, ldo, ldro, eps, dt, code, flags, index) -> int:
+    """Choose the workspace (and the grid schedule where it applies) and call ``fqkv_launch``
+    with device ``index`` current."""
+    if code == _lib.SCHED_AUTO and M <= _GRID_AUTO_MAX_M and _grid_preferred(M, H, N, dt, index):
+        tensors = [t for t in (x2, r2, g, w, rout2) if t is not None]
+        strides = [ldx, ldw] + ([ldr] if r2 is not None else []) + ([ldro] if rout2 is not None else [])
+        if _tma_ready(H, tensors, strides):
+            code = _lib.SCHED_GRID
+    key = (M, H, N, dt, code, index)
+    ws_bytes = _ws_bytes.get(key)
+    if ws_bytes is None:
+        ws_bytes = _ws_bytes[key] = _lib.workspace_bytes(M, H, N, dt, code)
+    stream = _current_stream(index)
+    if code == _lib.SCHED_GRID:
+        ws = _grid_workspace(index, stream, ws_bytes, x2.device)
+    else:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes > 0 else None
+    return _lib.launch(
+        x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), gcode, w.data_ptr(),
+        out2.data_ptr(), rout2.data_ptr() if rout2 is not None else None, M, H, N, ldx, ldr, ldw, ldo, ldro,
+        float(eps), dt, code, flags, ws.data_ptr() if ws is not None else None, ws_bytes, stream)
 
 
 def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, static_weights):
