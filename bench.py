@@ -22,7 +22,8 @@ residual add with the updated residual returned).  32 distinct seeded weight set
              (bf16, fp16), Qwen2-7B decode M=1/16/64 (with and without residual),
              Llama-3-70B M=1/16/256, the post-attention gate/up shape (N=28672), prefill
              M=512/2048/8192 (TFLOPS), the unfused PyTorch path (cuBLAS) on the same
-             inputs as the GPU comparator, a streaming-read bandwidth for context, and
+             inputs as the GPU comparator, an eager L2-flushed time of single Llama-3-8B
+             decode steps (M=1/16) as a cross-check, a streaming-read bandwidth for context, and
              the FP8-weight path (e4m3 weight, Llama-3-8B decode M=1/16), and a
              4-layer Llama-3-8B stack (M=1/16) unpatched vs the integration patch's
              modes (Q/K/V, + MLP gate/up, cross-layer, + one-launch Q/K/V rotary split).
@@ -372,6 +373,26 @@ def hbm_read_peak_gbs(dev) -> float:
     return gbs
 
 
+def eager_flushed_us(fn_step, n: int, dev) -> float:
+    """Median microseconds of one eager step timed alone with CUDA events, L2 flushed before
+    each: a 256 MB memset (twice the L2) runs first, which also keeps the GPU queue ahead
+    of the host, so the events bracket the step's kernels and not the host's launch cost.
+    A cross-check of the graph-timed numbers: no overlap with a preceding kernel, cold L2."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for i in range(n + 3):
+        flush.zero_()
+        e0.record()
+        fn_step(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if i >= 3:
+            times.append(e0.elapsed_time(e1) * 1e3)
+    del flush
+    return statistics.median(times)
+
+
 def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
     from triton_fused_rmsnorm_qkv import _lib
     from triton_fused_rmsnorm_qkv.kernel import schedule_info
@@ -396,6 +417,8 @@ def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
             t_ref = time_graph(torch_step_fn(ss, wl["eps"]), k, 5, dev) / k
             entry["torch_unfused_us"] = round(t_ref * 1e3, 3)
             entry["speedup_vs_torch_unfused"] = round(t_ref / t_ms, 2)
+            if mm <= 64:
+                entry["eager_l2_flushed_us"] = round(eager_flushed_us(op_step_fn(ss, wl["eps"], mm), 50, dev), 3)
         detail[label] = entry
         del ss
     detail.update(run_fp8w_detail(dev, peaks))
