@@ -188,10 +188,15 @@ def make_sets(wl: dict, M: int, dtype, dev, world: int, rank: int, sets: int):
     return out, layout
 
 
-def time_graph(fn_step, steps: int, warmup: int, dev, sampler: ClockSampler | None = None, barrier=None):
-    """Warm up, capture `steps` calls of fn_step(i) in one CUDA graph, replay it once timed.
+def time_graph(fn_step, steps: int, warmup: int, dev, sampler: ClockSampler | None = None, barrier=None,
+               replays: int = 1, min_seconds: float = 0.0, stats: dict | None = None):
+    """Warm up, capture `steps` calls of fn_step(i) in one CUDA graph, and time replays of it.
 
-    Returns milliseconds for the K steps (CUDA events on the capture stream)."""
+    Each replay is timed with its own CUDA events on the capture stream; the result is the
+    median over the replays, in milliseconds for the K steps.  At least `replays` replays
+    run, and more if needed to keep the GPU busy for `min_seconds` (so that a clock sampler
+    sees the load).  With `barrier`, the ranks meet before the first and after the last
+    replay.  `stats` (if given) receives the replay count and the first replay's time."""
     for i in range(warmup):
         fn_step(i)
     torch.cuda.synchronize(dev)
@@ -206,22 +211,37 @@ def time_graph(fn_step, steps: int, warmup: int, dev, sampler: ClockSampler | No
     torch.cuda.synchronize(dev)
     graph.replay()  # first replay uploads the graph
     torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if min_seconds > 0:  # size the replay count from one timed replay
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        replays = max(replays, int(math.ceil(min_seconds * 1e3 / max(e0.elapsed_time(e1), 1e-3))))
+    if barrier is not None:  # every rank runs the same number of replays
+        t = torch.tensor([replays], device=dev)
+        barrier(t)
+        replays = int(t.item())
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(replays)]
     if barrier:
         barrier()
     torch.cuda.synchronize(dev)
     ctx = sampler if sampler is not None else _Null()
     with ctx:
         with torch.cuda.stream(stream):
-            ev0.record(stream)
-            graph.replay()
-            ev1.record(stream)
+            for e0, e1 in evs:
+                e0.record(stream)
+                graph.replay()
+                e1.record(stream)
         torch.cuda.synchronize(dev)
     if barrier:
         barrier()
-    ms = ev0.elapsed_time(ev1)
+    times = [e0.elapsed_time(e1) for e0, e1 in evs]
+    if stats is not None:
+        stats.update(replays=replays, first_replay_ms=times[0], min_replay_ms=min(times), max_replay_ms=max(times))
     del graph
-    return ms
+    return statistics.median(times)
 
 
 class _Null:
@@ -244,32 +264,35 @@ def op_step_fn(sets, eps, M, schedule=None):
     return step
 
 
-def launches_per_step(M: int, H: int, dtype_code: int) -> int:
-    from triton_fused_rmsnorm_qkv import _lib
-
-    from triton_fused_rmsnorm_qkv.kernel import schedule_info
-
-    info = schedule_info(M, H, 6144, {_lib.BF16: torch.bfloat16, _lib.F16: torch.float16}[dtype_code])
-    return 2 if info["uses_prepass"] else 1
-
-
 # ----------------------------------------------------------------------------- CPU legs
-def cpu_time_op(wl: dict, M: int, dtype, seconds: float, threads: int, max_iters: int = 100000):
-    """Median seconds per op of the CPU oracle on one seeded set of the workload."""
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), or the platform's description."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or platform.machine()
+
+
+def cpu_time_op(wl: dict, M: int, dtype, seconds: float, threads: int):
+    """Median seconds per op of the CPU oracle on one seeded set of the workload, and the
+    number of ops timed: ``torch.utils.benchmark.Timer.blocked_autorange`` over about
+    ``seconds`` with ``threads`` threads."""
+    from torch.utils import benchmark
+
     sys.path.insert(0, str(ROOT))
     from oracle import forward, make_case
 
-    torch.set_num_threads(threads)
     N = wl["n_q"] * wl["d"] + 2 * wl["n_kv"] * wl["d"]
     x, r, g, w = make_case(M, wl["H"], N, dtype, 1000, wl["res"])
-    forward(x, r, g, w, wl["eps"])  # warm-up
-    times = []
-    t_end = time.perf_counter() + seconds
-    while time.perf_counter() < t_end and len(times) < max_iters:
-        t0 = time.perf_counter()
-        forward(x, r, g, w, wl["eps"])
-        times.append(time.perf_counter() - t0)
-    return statistics.median(times), len(times)
+    timer = benchmark.Timer(stmt="forward(x, r, g, w, eps)", num_threads=threads,
+                            globals=dict(forward=forward, x=x, r=r, g=g, w=w, eps=wl["eps"]))
+    m = timer.blocked_autorange(min_run_time=seconds)
+    return m.median, len(m.times) * m.number_per_run
 
 
 def run_reference(args, wl: dict, M: int) -> dict:
@@ -355,6 +378,64 @@ def torch_step_fn(sets, eps):
     return step
 
 
+def load_reference_triton():
+    """The reference's own package (its Triton kernels), installed unmodified under
+    baseline/_ref, imported under a private module name so that it cannot shadow this
+    repository's package of the same name.  None when it or Triton is not present."""
+    import importlib.util
+
+    pkg = ROOT / "baseline" / "_ref" / "triton_fused_rmsnorm_qkv"
+    if not (pkg / "__init__.py").exists():
+        return None
+    try:
+        import triton  # noqa: F401
+    except ImportError:
+        return None
+    name = "_reference_triton_fused_rmsnorm_qkv"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_reference_triton_detail(dev, peaks: dict, autotune: bool) -> dict:
+    """The reference's Triton kernels on this GPU, as a comparator outside the product path:
+    ``fused_rmsnorm_residual_matmul`` (autotuned on its first call per shape, during the
+    warm-up) or its ``_fixed`` variant, at Llama-3-8B M = 1 / 16 / 2048, graph-timed like the
+    other rows.  The reference returns no updated residual, so its bytes omit that write."""
+    ref = load_reference_triton()
+    if ref is None:
+        return {"unavailable": "the reference package (baseline/_ref) or Triton is not installed here"}
+    fn = ref.fused_rmsnorm_residual_matmul if autotune else ref.fused_rmsnorm_residual_matmul_fixed
+    out = {"entry_point": fn.__name__, "source": "baseline/_ref (the reference, installed unmodified)"}
+    for mm, n_sets in ((1, 32), (16, 32), (2048, 4)):
+        wl = dict(WORKLOADS["llama3-8b-decode"], sets=n_sets)
+        ss, layout = make_sets(wl, mm, torch.bfloat16, dev, 1, 0, n_sets)
+        H, N = wl["H"], layout.n_out
+
+        def step(i, ss=ss):
+            x, r, g, w = ss[i % len(ss)]
+            fn(x, r, g, w, wl["eps"])
+
+        k = 200 if mm <= 64 else 40
+        t0 = time.perf_counter()
+        try:
+            t_ms = time_graph(step, k, 3, dev) / k
+        except Exception as e:  # a Triton compile or launch problem on this part
+            out[f"M{mm}"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+            continue
+        b = algorithmic_bytes(mm, H, N, True) - 2 * mm * H  # no updated residual written
+        out[f"M{mm}"] = {"us": round(t_ms * 1e3, 3), "GB/s": round(b / t_ms / 1e6, 1),
+                         "pct_of_measured_hbm": round(100 * b / t_ms / 1e6 / peaks["hbm_gbs"], 2),
+                         "TFLOPS": round(2.0 * mm * N * H / t_ms / 1e9, 1),
+                         "setup_and_timing_s": round(time.perf_counter() - t0, 1)}
+        del ss
+    return out
+
+
 def hbm_read_peak_gbs(dev) -> float:
     """Streaming read bandwidth of a 4 GiB bf16 tensor (torch.sum), for context beside the
     measured copy peak: a decode op is almost entirely a read."""
@@ -393,7 +474,7 @@ def eager_flushed_us(fn_step, n: int, dev) -> float:
     return statistics.median(times)
 
 
-def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
+def run_detail(wl_default: dict, dev, peaks: dict, args_triton_comparator: str = "autotune") -> dict:
     from triton_fused_rmsnorm_qkv import _lib
     from triton_fused_rmsnorm_qkv.kernel import schedule_info
 
@@ -422,7 +503,10 @@ def run_detail(wl_default: dict, dev, peaks: dict) -> dict:
         detail[label] = entry
         del ss
     detail.update(run_fp8w_detail(dev, peaks))
+    if args_triton_comparator != "off":
+        detail["reference_triton"] = run_reference_triton_detail(dev, peaks, args_triton_comparator == "autotune")
     detail["llama3-8b_layer_stack"] = run_layer_stack(dev)
+    detail["llama3-8b_kv_cache_decode"] = run_kv_decode(dev)
     return detail
 
 
@@ -493,7 +577,182 @@ def run_layer_stack(dev, n_layers: int = 4, ms=(1, 16), steps: int = 50) -> dict
     return out
 
 
+def run_kv_decode(dev, n_layers: int = 4, batches=(1, 16), prompt_len: int = 128, n_new: int = 256,
+                  repeats: int = 3) -> dict:
+    """Greedy decode with a static KV cache on a Llama-3-8B-shaped model (random init, bf16,
+    ``n_layers`` decoder layers, full vocabulary): the methodology of the reference's
+    e2e_decode.py (prompt 128, 256 new tokens, batch 1 and 16, tokens per second over the
+    decode phase) with each decode step replayed from a CUDA graph
+    (integration.GraphedGreedyDecoder).  Unpatched against the patch's modes; each patched
+    run's tokens are compared with the unpatched run's."""
+    from contextlib import nullcontext
+
+    from integration import GraphedGreedyDecoder, build_llama3_8b, fused_patch
+
+    model = build_llama3_8b(dtype=torch.bfloat16, device=str(dev), num_hidden_layers=n_layers)
+    modes = (("unpatched", None), ("qkv", {}), ("cross-layer+rope", {"cross_layer": True, "rope": True}))
+    out = {"layers": n_layers, "prompt_len": prompt_len, "new_tokens": n_new,
+           "unit": "decode tokens per second (batch x steps / CUDA-event time of the graph replays)"}
+    with torch.no_grad():
+        for B in batches:
+            gen = torch.Generator(device=dev).manual_seed(11)
+            prompt = torch.randint(0, model.config.vocab_size, (B, prompt_len), generator=gen, device=dev)
+            row, ref_tokens = {}, None
+            for name, kw in modes:
+                with (nullcontext() if kw is None else fused_patch(model, **kw)):
+                    dec = GraphedGreedyDecoder(model, B, prompt_len + n_new)
+                    secs = []
+                    for _ in range(repeats):
+                        tokens = dec.generate(prompt, n_new)
+                        secs.append(dec.decode_seconds)
+                steps = n_new - 2
+                t = statistics.median(secs)
+                entry = {"tok_per_s": round(B * steps / t, 1), "us_per_step": round(t / steps * 1e6, 2)}
+                if ref_tokens is None:
+                    ref_tokens = tokens
+                else:
+                    same = (tokens == ref_tokens).all(dim=0)
+                    entry["tokens_equal_unpatched"] = bool(same.all())
+                    entry["steps_equal_before_first_difference"] = int(same.long().cumprod(0).sum())
+                row[name] = entry
+            out[f"batch{B}"] = row
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------------------------- GPU arm
+# Llama-3-70B rows of the head-sharded run (N > 1): (label, M, weight sets).
+SHARDED_DETAIL = [("llama3-70b_M1", 1, 16), ("llama3-70b_M16", 16, 16), ("llama3-70b_M256", 256, 8)]
+
+
+def reference_unsharded(wl: dict, M: int, dtype, dev):
+    """Set 0 of make_sets with the whole (unsharded) weight, rebuilt from the same seed."""
+    gen = torch.Generator(device=dev).manual_seed(1000)
+    torch.randn(1, M, wl["H"], generator=gen, device=dev)
+    if wl["res"]:
+        torch.randn(1, M, wl["H"], generator=gen, device=dev)
+    torch.randn(wl["H"], generator=gen, device=dev)
+    N = wl["n_q"] * wl["d"] + 2 * wl["n_kv"] * wl["d"]
+    return (0.02 * torch.randn(N, wl["H"], generator=gen, device=dev)).to(dtype)
+
+
+def shard_check(pg, sets, layout, wl: dict, M: int, dtype, dev, rank: int, world: int):
+    """Untimed check of a head-sharded step: every rank computes set 0 of its shard, an NCCL
+    all-gather reassembles Q/K/V, and rank 0 compares it with the unsharded op.  The updated
+    residual (computed by every rank from replicated inputs) must be bit-identical."""
+    from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul, fused_rmsnorm_residual_matmul
+    from triton_fused_rmsnorm_qkv.sharding import gather_qkv
+
+    x, r, g, w_loc = sets[0]
+    out_loc, hid_loc = fused_add_rmsnorm_matmul(x, r, g, w_loc, wl["eps"])
+    full = gather_qkv(out_loc, layout)
+    hids = [torch.empty_like(hid_loc) for _ in range(world)]
+    pg.all_gather(hids, hid_loc.contiguous())
+    result = None
+    if rank == 0:
+        ref = fused_rmsnorm_residual_matmul(x, r, g, reference_unsharded(wl, M, dtype, dev), wl["eps"])
+        d = full.float() - ref.float()
+        result = {"max_abs_vs_unsharded": float(d.abs().max()),
+                  "rel_l2_vs_unsharded": float(d.norm() / ref.float().norm()),
+                  "residual_bit_identical_across_ranks":
+                      all(torch.equal(h.view(torch.int16), hids[0].view(torch.int16)) for h in hids),
+                  "gathered_with": "nccl all_gather"}
+    pg.barrier()
+    return result
+
+
+def run_sharded_detail(pg, barrier, dev, rank: int, world: int, peaks: dict) -> dict:
+    """Llama-3-70B layer head-sharded over the ranks at M = 1 / 16 / 256: graph-timed like the
+    headline (max over ranks), aggregate and per-GPU throughput, and a shard check each."""
+    from triton_fused_rmsnorm_qkv import _lib
+    from triton_fused_rmsnorm_qkv.kernel import schedule_info
+
+    out = {}
+    for label, mm, n_sets in SHARDED_DETAIL:
+        wl = dict(WORKLOADS["llama3-70b"], sets=n_sets)
+        ss, layout = make_sets(wl, mm, torch.bfloat16, dev, world, rank, n_sets)
+        H, N_glob, N_loc = wl["H"], layout.n_out, ss[0][3].shape[0]
+        k = 200 if mm <= 64 else 50
+        t = torch.tensor([time_graph(op_step_fn(ss, wl["eps"], mm), k, 5, dev, barrier=barrier, replays=20) / k],
+                         device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        t_ms = float(t.item())
+        b_rank = algorithmic_bytes(mm, H, N_loc, True)
+        fl_rank = 2.0 * mm * N_loc * H
+        entry = {"M": mm, "H": H, "N": N_glob, "N_per_gpu": N_loc, "us": round(t_ms * 1e3, 3),
+                 "GB/s_aggregate": round(world * b_rank / t_ms / 1e6, 1), "GB/s_per_gpu": round(b_rank / t_ms / 1e6, 1),
+                 "pct_of_measured_hbm_per_gpu": round(100 * b_rank / t_ms / 1e6 / peaks["hbm_gbs"], 2),
+                 "TFLOPS_aggregate": round(world * fl_rank / t_ms / 1e9, 1),
+                 "TFLOPS_per_gpu": round(fl_rank / t_ms / 1e9, 1),
+                 "pct_of_measured_bf16_per_gpu": round(100 * fl_rank / t_ms / 1e9 / peaks["bf16_tflops"], 2),
+                 "schedule": _lib.SCHEDULE_NAMES[schedule_info(mm, H, N_loc)["schedule"]]}
+        chk = shard_check(pg, ss, layout, wl, mm, torch.bfloat16, dev, rank, world)
+        if chk is not None:
+            entry["shard_check"] = chk
+        out[label] = entry
+        del ss
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_e2e(sets, wl: dict, M: int, H: int, N_loc: int, dtype, dev, args, pg) -> dict:
+    """The metric through the public API on every rank: each step copies that step's x and
+    residual from pinned host memory to the device, runs the op on the rank's shard and
+    copies its output and updated residual back, synchronising every step.  Time per step
+    is the max over ranks of the CUDA-event (or, if longer, wall-clock) time."""
+    from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul
+
+    x0, r0, g0, w0 = sets[0]
+    xh = x0.cpu().pin_memory()
+    rh = r0.cpu().pin_memory() if r0 is not None else None
+    out_h = torch.empty(1, M, N_loc, dtype=dtype).pin_memory()
+    hid_h = torch.empty(1, M, H, dtype=dtype).pin_memory()
+    xd, rd = torch.empty_like(x0), (torch.empty_like(r0) if r0 is not None else None)
+    e2e_steps = max(10, min(args.steps, 2000))
+
+    def e2e_step(i):
+        _, _, g_i, w_i = sets[i % len(sets)]
+        xd.copy_(xh, non_blocking=True)
+        if rd is not None:
+            rd.copy_(rh, non_blocking=True)
+        out, hid = fused_add_rmsnorm_matmul(xd, rd, g_i, w_i, wl["eps"], static_weights=True)
+        out_h.copy_(out, non_blocking=True)
+        hid_h.copy_(hid, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    for i in range(max(3, args.warmup)):
+        e2e_step(i)
+    if pg is not None:
+        pg.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    ev0.record()
+    w0t = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - w0t
+    t = torch.tensor([max(ev0.elapsed_time(ev1), wall * 1e3) / e2e_steps], device=dev)
+    world = 1
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        world = pg.get_world_size()
+    e2e_ms = float(t.item())
+    h2d = xh.numel() * 2 + (rh.numel() * 2 if rh is not None else 0)
+    d2h = out_h.numel() * 2 + hid_h.numel() * 2
+    job_bytes = algorithmic_bytes(M, H, N_loc, wl["res"]) * world
+    return {"value": round(job_bytes / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+            "h2d_bytes_per_step_per_gpu": h2d, "d2h_bytes_per_step_per_gpu": d2h,
+            "ms_per_step": round(e2e_ms, 6), "steps": e2e_steps,
+            "path": "fused_add_rmsnorm_matmul (public API) on every rank: pinned host x/residual in, the rank's "
+                    "output and updated residual back, synchronised every step; job bytes over the max-over-ranks "
+                    "time",
+            "n_gpus_used": world}
+
+
 def run_ours(args, wl: dict, M: int) -> dict | None:
     world, rank, local = dist_env()
     dev = torch.device("cuda", local)
@@ -522,8 +781,13 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
             os.close(saved_stdout)
         pg = dist
 
-    def barrier():
-        if pg is not None:
+    def barrier(t=None):
+        """Meet the other ranks; with a tensor, also take its max over the ranks."""
+        if pg is None:
+            return
+        if t is not None:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        else:
             pg.barrier()
 
     dtype = torch.bfloat16
@@ -532,10 +796,13 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
     N_loc = sets[0][3].shape[0]
     peaks = measured_peaks()
 
-    # ---- main timed region
+    # ---- main timed region: the K-step graph replayed (at least 50 times, and for at least
+    # 0.3 s so the clock sampler sees the load); median replay, max over ranks
     sampler = ClockSampler(local)
     step = op_step_fn(sets, wl["eps"], M)
-    ms = time_graph(step, args.steps, args.warmup, dev, sampler=sampler, barrier=barrier)
+    tstats: dict = {}
+    ms = time_graph(step, args.steps, args.warmup, dev, sampler=sampler, barrier=barrier, replays=50,
+                    min_seconds=0.3, stats=tstats)
     t = torch.tensor([ms], device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -551,101 +818,58 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
     from triton_fused_rmsnorm_qkv.kernel import schedule_info
 
     sched = schedule_info(M, H, N_loc)
-    launches = args.steps * (2 if sched["uses_prepass"] else 1)
+    launches = tstats["replays"] * args.steps * (2 if sched["uses_prepass"] else 1)
 
     # ---- verification of the sharded run (untimed): NCCL all-gather vs unsharded op
-    shard_check = None
-    if world > 1:
-        from triton_fused_rmsnorm_qkv import fused_rmsnorm_residual_matmul
-        from triton_fused_rmsnorm_qkv.sharding import gather_qkv
+    check = shard_check(pg, sets, layout, wl, M, dtype, dev, rank, world) if world > 1 else None
 
-        from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul as _fused_add
+    # ---- e2e through the public API with pinned host buffers, on every rank
+    e2e = run_e2e(sets, wl, M, H, N_loc, dtype, dev, args, pg)
 
-        x, r, g, w_loc = sets[0]
-        out_loc, hid_loc = _fused_add(x, r, g, w_loc, wl["eps"])
-        full = gather_qkv(out_loc, layout)
-        # Every rank computes the same updated residual from replicated inputs: gather them
-        # and require bit equality.
-        hids = [torch.empty_like(hid_loc) for _ in range(world)]
-        pg.all_gather(hids, hid_loc.contiguous())
-        hid_same = all(torch.equal(h.view(torch.int16), hids[0].view(torch.int16)) for h in hids)
-        if rank == 0:
-            gen = torch.Generator(device=dev).manual_seed(1000)
-            torch.randn(1, M, H, generator=gen, device=dev)
-            if wl["res"]:
-                torch.randn(1, M, H, generator=gen, device=dev)
-            torch.randn(H, generator=gen, device=dev)
-            w_full = (0.02 * torch.randn(N_glob, H, generator=gen, device=dev)).to(dtype)
-            ref = fused_rmsnorm_residual_matmul(x, r, g, w_full, wl["eps"])
-            d = (full.float() - ref.float())
-            shard_check = {"max_abs_vs_unsharded": float(d.abs().max()),
-                           "rel_l2_vs_unsharded": float(d.norm() / ref.float().norm()),
-                           "residual_bit_identical_across_ranks": bool(hid_same),
-                           "gathered_with": "nccl all_gather"}
-        barrier()
+    # ---- Llama-3-70B head-sharded rows (N > 1)
+    sharded = run_sharded_detail(pg, barrier, dev, rank, world, peaks) if world > 1 and not args.no_detail else {}
 
     if rank != 0:
         if pg is not None:
             pg.destroy_process_group()
         return None
 
-    # ---- e2e through the public API with pinned host buffers
-    from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul
-
-    x0, r0, g0, w0 = sets[0]
-    xh = x0.cpu().pin_memory()
-    rh = r0.cpu().pin_memory() if r0 is not None else None
-    out_h = torch.empty(1, M, N_loc, dtype=dtype).pin_memory()
-    hid_h = torch.empty(1, M, H, dtype=dtype).pin_memory()
-    xd, rd = torch.empty_like(x0), (torch.empty_like(r0) if r0 is not None else None)
-    e2e_steps = max(10, min(args.steps, 2000))
-
-    def e2e_step(i):
-        _, _, g_i, w_i = sets[i % len(sets)]
-        xd.copy_(xh, non_blocking=True)
-        if rd is not None:
-            rd.copy_(rh, non_blocking=True)
-        out, hid = fused_add_rmsnorm_matmul(xd, rd, g_i, w_i, wl["eps"], static_weights=True)
-        out_h.copy_(out, non_blocking=True)
-        hid_h.copy_(hid, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
-
-    for i in range(max(3, args.warmup)):
-        e2e_step(i)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(dev)
-    ev0.record()
-    w0t = time.perf_counter()
-    for i in range(e2e_steps):
-        e2e_step(i)
-    ev1.record()
-    torch.cuda.synchronize(dev)
-    wall = time.perf_counter() - w0t
-    e2e_ms = max(ev0.elapsed_time(ev1), wall * 1e3) / e2e_steps
-    h2d = xh.numel() * 2 + (rh.numel() * 2 if rh is not None else 0)
-    d2h = out_h.numel() * 2 + hid_h.numel() * 2
-    e2e = {"value": round(per_rank / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 6),
-           "path": "fused_add_rmsnorm_matmul (public API) with pinned host x/residual in, out/hidden back, "
-                   "synchronised every step", "n_gpus_used": 1}
-
     # ---- detail: the metric's other points and the other configs, timed the same way,
     # with the unfused PyTorch path (cuBLAS) as the GPU comparator (N=1 only)
     detail = {}
     if world == 1 and not args.no_detail:
-        detail = run_detail(wl, dev, peaks)
+        detail = run_detail(wl, dev, peaks, args.triton_comparator)
         torch.cuda.empty_cache()
+    detail.update(sharded)
 
-    # ---- CPU baseline (rank 0, N=1): the oracle on a bounded sample
+    # ---- CPU baseline (rank 0, N=1): the oracle on a bounded sample, all host threads and one
     cpu = None
     if world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         sec, n = cpu_time_op(wl, M, dtype, args.cpu_seconds, threads)
-        cpu = {"value": round(algorithmic_bytes(M, H, N_glob, wl["res"]) / sec / 1e9, 3), "unit": "GB/s",
-               "cores": threads, "kind": "port",
-               "sample": f"{n} ops of the same workload (M={M}, H={H}, N={N_glob}, bf16, one seeded set) "
-                         f"over ~{args.cpu_seconds:.0f} s, median op time {sec * 1e3:.3f} ms"}
+        sec1, n1 = cpu_time_op(wl, M, dtype, max(2.0, args.cpu_seconds / 3), 1)
+        b_glob = algorithmic_bytes(M, H, N_glob, wl["res"])
+        cpu = {"value": round(b_glob / sec / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "one_thread_value": round(b_glob / sec1 / 1e9, 3), "cpu_model": cpu_model(),
+               "torch_threads": threads,
+               "method": "torch.utils.benchmark.Timer.blocked_autorange, median",
+               "sample": f"{n} ops of the same workload (M={M}, H={H}, N={N_glob}, bf16, one seeded set) over "
+                         f"~{args.cpu_seconds:.0f} s on {threads} threads, median op {sec * 1e3:.3f} ms; "
+                         f"{n1} ops on 1 thread, median op {sec1 * 1e3:.3f} ms"}
 
+    # ncu DRAM bytes of the dominant kernel, captured at N = 1 on the whole weight; at N > 1
+    # a rank reads 1/N of the weight, so the capture is scaled by this rank's algorithmic bytes.
+    def traffic(name: str):
+        t1 = profile_traffic(name)
+        if t1 is None:
+            return None
+        if world == 1:
+            return t1
+        return int(round(t1 * per_rank / algorithmic_bytes(M, H, N_glob, wl["res"])))
+
+    traffic_note = ("ncu dram__bytes_read.sum + dram__bytes_write.sum per launch" if world == 1 else
+                    f"ncu DRAM bytes of the N=1 capture scaled to this rank's share ({per_rank} of "
+                    f"{algorithmic_bytes(M, H, N_glob, wl['res'])} algorithmic bytes)")
     if sched["schedule"] == _lib.SCHED_PREFILL:
         # Tensor-bound: FLOPs of the step over its time (pre-pass + GEMM), against the
         # measured cuBLAS bf16 burst peak.
@@ -654,20 +878,21 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)",
-                "traffic": profile_traffic(f"prefill_gemm_pair_llama3-8b_m{M}"),
+                "traffic": traffic(f"prefill_gemm_pair_llama3-8b_m{M}"), "traffic_source": traffic_note,
                 "kernel": f"norm_prepass_kernel + {gemm}; time of the whole step"}
     else:
         achieved = per_rank / step_s / 1e9
         kernel = {_lib.SCHED_DECODE: "decode_kernel (fused swap-AB tcgen05, cluster split-K)",
+                  _lib.SCHED_GRID: "decode_kernel GRID variant (fused swap-AB tcgen05, K split over CTAs)",
                   _lib.SCHED_SPLIT: "norm_prepass_kernel + streamk_kernel; time of the whole step"}.get(
                       sched["schedule"], "simt_kernel")
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)",
                 "pct_of_8TBs_spec": round(100 * achieved / HBM_SPEC_GBS, 2),
-                "traffic": profile_traffic(f"decode_llama3-8b_m{M}") if sched["schedule"] == _lib.SCHED_DECODE
-                else None,
-                "kernel": kernel}
+                "traffic": traffic(f"decode_llama3-8b_m{M}")
+                if sched["schedule"] in (_lib.SCHED_DECODE, _lib.SCHED_GRID) else None,
+                "traffic_source": traffic_note, "kernel": kernel}
 
     line = {
         "metric": METRIC,
@@ -690,7 +915,10 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
                    "l2": f"{wl['sets']} rotating weight sets ({wl['sets'] * N_loc * H * 2 / 1e9:.2f} GB per GPU) "
                          f"> 126 MB L2",
                    "parallelism": f"tp{world} (column-parallel by heads)" if world > 1 else "single GPU",
-                   "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
+                   "timing": f"K steps in one CUDA graph, replayed {tstats['replays']} times with CUDA events per "
+                             f"replay; median replay, max over ranks",
+                   "replays": tstats["replays"],
+                   "replay_ms": {k: round(v, 6) for k, v in tstats.items() if k.endswith("_ms")},
                    "schedule": {k: v for k, v in sched.items()}},
         "gpu_launches": launches,
         "clocks": sampler.summary(),
@@ -700,11 +928,47 @@ def run_ours(args, wl: dict, M: int) -> dict | None:
     }
     if detail:
         line["detail"] = detail
-    if shard_check:
-        line["shard_check"] = shard_check
+    if check:
+        line["shard_check"] = check
     if pg is not None:
         pg.destroy_process_group()
     return line
+
+
+def run_profile_case(args) -> int:
+    """``--profile-case``: a small fixed workload of the fused op for a profiler capture.
+
+    Seeded x / residual ~ N(0, 1), gains 1 + 0.1 N(0, 1) and weights N(0, 0.02) on cuda:0;
+    ``--calls`` eager calls of ``fused_add_rmsnorm_matmul`` (or, with ``--fp8w``,
+    ``fused_add_rmsnorm_matmul_fp8w`` on weights quantised by ``quantize_weight_e4m3``)
+    rotate over ``--sets`` weight sets (default 4), so that with weights larger than a
+    quarter of L2 each captured launch reads its weight from HBM.  Prints one line with a
+    checksum of the last output.  No timing is printed: numbers taken under a profiler are
+    not benchmark values."""
+    from triton_fused_rmsnorm_qkv import (fused_add_rmsnorm_matmul, fused_add_rmsnorm_matmul_fp8w,
+                                          quantize_weight_e4m3)
+
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    dev = torch.device("cuda", 0)
+    H, N, M, n_sets = args.H, args.N, args.m or 16, args.sets or 4
+    g = torch.Generator(device=dev).manual_seed(5)
+    sets = []
+    for _ in range(n_sets):
+        gain = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(dt)
+        w = (0.02 * torch.randn(N, H, generator=g, device=dev)).to(dt)
+        sets.append((gain, quantize_weight_e4m3(w) if args.fp8w else w))
+    x = torch.randn(1, M, H, generator=g, device=dev).to(dt)
+    r = torch.randn(1, M, H, generator=g, device=dev).to(dt)
+    out = None
+    for i in range(args.calls):
+        gain, w = sets[i % n_sets]
+        if args.fp8w:
+            out, _ = fused_add_rmsnorm_matmul_fp8w(x, r, gain, w[0], w[1], 1e-5, static_weights=True)
+        else:
+            out, _ = fused_add_rmsnorm_matmul(x, r, gain, w, 1e-5, schedule=args.schedule, static_weights=True)
+    torch.cuda.synchronize()
+    print(f"ok M={M} H={H} N={N} calls={args.calls} checksum={float(out.float().abs().sum()):.6e}")
+    return 0
 
 
 def main() -> int:
@@ -718,9 +982,22 @@ def main() -> int:
     ap.add_argument("--no-detail", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--triton-comparator", choices=("autotune", "fixed", "off"), default="autotune",
+                    help="the reference's Triton kernels as a detail comparator (from baseline/_ref)")
     ap.add_argument("--sets", type=int, default=None,
                     help="rotating weight sets (default: the workload's; fewer only for profiling captures)")
+    prof = ap.add_argument_group("profiler workload (--profile-case)")
+    prof.add_argument("--profile-case", action="store_true",
+                      help="run a small fixed workload for an ncu capture instead of the benchmark")
+    prof.add_argument("--H", type=int, default=4096)
+    prof.add_argument("--N", type=int, default=6144)
+    prof.add_argument("--schedule", default=None, help="auto (default), decode, grid, split, prefill or simt")
+    prof.add_argument("--dtype", choices=("bf16", "fp16"), default="bf16")
+    prof.add_argument("--fp8w", action="store_true", help="e4m3 weights with an fp32 scale per row")
+    prof.add_argument("--calls", type=int, default=8)
     args = ap.parse_args()
+    if args.profile_case:
+        return run_profile_case(args)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     wl = dict(WORKLOADS[args.workload])

@@ -19,6 +19,7 @@
 namespace fqkv {
 
 __device__ int g_status = 0;
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
 
 namespace {
 
@@ -230,7 +231,7 @@ int validate(const Problem& p) {
     return fail(FQKV_ERR_SHAPE, "a row stride is smaller than its row length");
   if (p.schedule < FQKV_SCHED_AUTO || p.schedule > FQKV_SCHED_GRID)
     return fail(FQKV_ERR_SCHEDULE, "unknown schedule %d", p.schedule);
-  if (p.flags & ~(FQKV_FLAG_PDL | FQKV_FLAG_STATIC_WEIGHTS))
+  if (p.flags & ~(FQKV_FLAG_PDL | FQKV_FLAG_STATIC_WEIGHTS | FQKV_FLAG_TEST_WITHHOLD))
     return fail(FQKV_ERR_SCHEDULE, "unknown flag bits 0x%x", p.flags);
   const int64_t xb = mat_bytes(p.M, p.H, p.ldx), ob = mat_bytes(p.M, p.N, p.ldo);
   const int64_t wb = p.w16 ? mat_bytes(p.N, p.H, p.ldw) : 0;  // 0: overlaps() ignores it
@@ -241,12 +242,16 @@ int validate(const Problem& p) {
   if (overlaps(p.rout, rob, p.x, xb) || overlaps(p.rout, rob, p.r, rb) || overlaps(p.rout, rob, p.w, wb))
     return fail(FQKV_ERR_ALIAS, "residual_out overlaps an input (in-place update is not supported)");
   const int sched = choose_schedule(p);
+  if (sched == FQKV_SCHED_SIMT && (p.flags & FQKV_FLAG_TEST_WITHHOLD))
+    return fail(FQKV_ERR_SCHEDULE, "FQKV_FLAG_TEST_WITHHOLD applies to the decode and grid schedules only");
   if (sched != FQKV_SCHED_SIMT) {
     if (!tma_eligible(p))
       return fail(FQKV_ERR_ALIGN,
                   "schedule %d needs H %% 8 == 0, H <= %lld, row strides %% 8 == 0 and 16-byte aligned x, "
                   "residual, rms_weight, weight and residual_out",
                   sched, (long long)kPrepassMaxH);
+    if ((p.flags & FQKV_FLAG_TEST_WITHHOLD) && sched != FQKV_SCHED_DECODE && sched != FQKV_SCHED_GRID)
+      return fail(FQKV_ERR_SCHEDULE, "FQKV_FLAG_TEST_WITHHOLD applies to the decode and grid schedules only");
     if (sched == FQKV_SCHED_DECODE && p.M > kFusedMaxM)
       return fail(FQKV_ERR_SCHEDULE, "the decode schedule takes at most %lld rows (M = %lld)",
                   (long long)kFusedMaxM, (long long)p.M);
@@ -290,6 +295,25 @@ using namespace fqkv;
 
 extern "C" FQKV_API int fqkv_version(void) { return 102; }
 
+#ifdef FQKV_TRACE
+// Profiling builds only: the timeline buffer the kernels' trace points write to
+// (fqkv_device.cuh), kTraceSlots 64-bit words per CTA record.
+namespace fqkv {
+__device__ unsigned long long* g_trace_buf = nullptr;
+__device__ unsigned int g_trace_cap = 0;
+__device__ unsigned int g_trace_ctr = 0;
+}  // namespace fqkv
+
+extern "C" FQKV_API int fqkv_trace_attach(void* buf, unsigned int records) {
+  unsigned long long* b = static_cast<unsigned long long*>(buf);
+  const unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyToSymbol(g_trace_buf, &b, sizeof(b));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_trace_cap, &records, sizeof(records));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_trace_ctr, &zero, sizeof(zero));
+  return e == cudaSuccess ? 0 : cuda_fail(e, "fqkv_trace_attach");
+}
+#endif
+
 // The projection's [M, (n_q + 2 n_kv) d] output to head-major Q, K, V with the rotary
 // embedding on Q and K (fqkv_rope.cu): what llama3_patch.py:156-168 does in PyTorch after
 // the fused call (split, view as heads, transpose, apply_rotary_pos_emb).
@@ -303,6 +327,8 @@ extern "C" FQKV_API int fqkv_launch_fp8w(const void* x, const void* residual, co
                                          int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro, float eps, int dtype,
                                          int flags, void* stream) {
   if (!weight || !weight_scale) return fail(FQKV_ERR_NULL, "weight and weight_scale must be non-null");
+  if (flags & FQKV_FLAG_TEST_WITHHOLD)
+    return fail(FQKV_ERR_SCHEDULE, "FQKV_FLAG_TEST_WITHHOLD applies to fqkv_launch only");
   // The rest is checked as fqkv_launch checks it, on the decode schedule; the one-byte
   // weight's layout and aliasing are checked here.
   Problem p{M, H, N, ldx, ldr, ldw, ldo, ldro, x, residual, rms_weight, nullptr, out, residual_out,
@@ -486,6 +512,22 @@ extern "C" FQKV_API int fqkv_device_status(void* stream, int* status) {
   return 0;
 }
 
+extern "C" FQKV_API int fqkv_test_set_wait_limit_ns(unsigned long long ns) {
+  const unsigned long long v = ns ? ns : kWaitLimitNs;
+  const cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v));
+  return e == cudaSuccess ? 0 : cuda_fail(e, "cudaMemcpyToSymbol(wait limit)");
+}
+
+extern "C" FQKV_API int fqkv_stream_capture_id(void* stream, unsigned long long* id) {
+  if (!id) return fail(FQKV_ERR_NULL, "id must be non-null");
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  unsigned long long cid = 0;
+  const cudaError_t e = cudaStreamGetCaptureInfo(static_cast<cudaStream_t>(stream), &status, &cid);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamGetCaptureInfo");
+  *id = status == cudaStreamCaptureStatusActive ? cid : 0ull;
+  return 0;
+}
+
 extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const void* rms_weight, int rms_weight_dtype,
                            const void* weight, void* out, void* residual_out, int64_t M, int64_t H, int64_t N,
                            int64_t ldx, int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro, float eps, int dtype,
@@ -612,17 +654,17 @@ extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const v
 //
 // Some callers cannot allocate device memory when they run the op: an inference
 // engine's plugin whose enqueue step must not allocate (the engine owns all memory and
-// forbids the implicit device synchronisation cudaMalloc can cause), a runtime with a
-// fixed memory budget that allocates nothing after start-up, or code running while a
-// stream is being captured.  They cannot hand fqkv_launch the workspace its pre-pass
+// forbids the implicit device synchronisation cudaMalloc can cause), or a runtime with a
+// fixed memory budget that allocates nothing after start-up.  They cannot hand
+// fqkv_launch the workspace its pre-pass
 // schedule needs, so fqkv_launch_noalloc runs that schedule (norm pre-pass + stream-K
 // GEMM) on a fixed array of device memory that belongs to the library.
 //
 // The array is a file-scope __device__ variable: every GPU that loads the library holds
 // its own copy (kNoAllocScratchBytes, about 5.5 MB) until the process exits.  Its
 // device address is looked up with cudaGetSymbolAddress the first time the entry point
-// runs on a device (with that device current); make that first call before capturing a
-// stream.  All calls on a device share the array and it keeps the last call's contents:
+// runs on a device in a CUDA context (with that device and context current); make that
+// first call before capturing a stream.  All calls on a device share the array and it keeps the last call's contents:
 // the pre-pass zeroes the arrival counters each call, the other regions are fully
 // rewritten before they are read.  Calls whose kernels overlap on the GPU (e.g. issued
 // on two streams at once) race on the array and must be serialised by the caller.
@@ -640,23 +682,43 @@ constexpr size_t kNoAllocScratchBytes = kNoAllocNormedBytes + kNoAllocPartialByt
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// Symbol addresses belong to a CUDA context: the address is cached per (device, context),
+// so a caller that makes another context current on the same device gets that context's
+// copy of the array.  The current context comes from the driver (cuCtxGetCurrent, reached
+// through the runtime so the library does not link libcuda).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {};
+std::map<std::pair<int, CUcontext>, void*> g_noalloc_ptr;
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+std::once_flag g_ctx_once;
 
-// Device address of this device's copy of g_noalloc_scratch (looked up once per device).
+// Device address of this device's (and context's) copy of g_noalloc_scratch, looked up once.
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(FQKV_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::call_once(g_ctx_once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  if (!g_ctx_get_current) return fail(FQKV_ERR_DEVICE, "cuCtxGetCurrent is not available from the driver");
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx)
+    return fail(FQKV_ERR_DEVICE, "no current CUDA context on device %d", dev);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  const auto key = std::make_pair(dev, ctx);
+  auto it = g_noalloc_ptr.find(key);
+  if (it == g_noalloc_ptr.end()) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(scratch)");
-    g_noalloc_ptr[dev] = p;
+    it = g_noalloc_ptr.emplace(key, p).first;
   }
-  *out = g_noalloc_ptr[dev];
+  *out = it->second;
   return 0;
 }
 

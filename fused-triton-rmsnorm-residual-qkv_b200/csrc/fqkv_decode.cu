@@ -145,6 +145,7 @@ template <typename T, int MPAD, int NT, bool F8, bool GRID>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmW, const DecodeParams p, const int stages) {
   extern __shared__ uint8_t smem_raw[];
+  FQKV_TRACE_DECL
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Layout L = make_layout(stages, NT, MPAD, p.nkb_max, F8);
   uint8_t* ring = smem + L.ring;
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kBoxTiles = decode_box_tiles(NT);
 
   // ---------------------------------------------------------------- setup
+  FQKV_TRACE_BEGIN();
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -217,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   if (threadIdx.x == 0) pdl_launch_dependents();
+  if (threadIdx.x == 0) FQKV_TRACE_POINT(3);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -233,7 +236,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0, round = 0, issued = 0;
       const int nstage = F8 ? (nkb + 1) / 2 : nkb;  // e4m3: a ring stage holds two k-blocks
       for (int i = 0; i < nstage; ++i) {
-        if (i == pre) ok = mbar_wait(acts_bar, 0);
+        if (i == pre) {
+          ok = mbar_wait(acts_bar, 0);
+          FQKV_TRACE_POINT(5);
+        }
         if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
         mbar_arrive_expect_tx(&full[s], tx);
         // A stage holds NT 128-row tiles: one box of NT x 128 rows for NT <= 2, else NT
@@ -242,12 +248,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < NT; j += kBoxTiles)
           tma_load_2d_hint(ring + s * L.stage_bytes + j * kWTileBytes, &tmW, &full[s],
                            (kb0 + (F8 ? 2 * i : i)) * kKBlock, n_base + j * kTileRows, pol_w);
+        if (i == 0) FQKV_TRACE_POINT(4);
         ++issued;
         if (++s == stages) {
           s = 0;
           ++round;
         }
       }
+      FQKV_TRACE_POINT(6);
       // Before leaving, make sure none of this CTA's loads is still in flight: the last
       // `stages` loads are the only ones that can be (bounded waits).
       for (int j = max(0, issued - stages); j < issued; ++j) mbar_wait(&full[j % stages], (j / stages) & 1);
@@ -279,6 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int i = 0; i < (F8 ? 0 : nkb) && ok; ++i) {
         if (!(ok = mbar_wait(&full[s], round & 1))) break;
+        if (i == 0) FQKV_TRACE_POINT(11);
+        if (i == nkb - 1) FQKV_TRACE_POINT(12);
         tc_fence_after();
         const uint32_t a_base = smem_u32(ring + s * L.stage_bytes);
         const uint32_t b_base = smem_u32(normed + i * MPAD * 128);
@@ -351,6 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     pdl_wait();
+    if (et == 0) FQKV_TRACE_POINT(7);
     if (!static_w) issue_gain();
     // Pass 1: warp nw takes rows nw, nw + 8, nw + 16, ... two at a time; each lane issues
     // up to kLoadBatch chunk loads of x (and r) per row before consuming any, so a pair of
@@ -484,6 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("bar.sync 1, 256;" ::: "memory");
     // Every activation load has returned: the producer may now fill the whole ring.
     if (et == 0) mbar_arrive(acts_bar);
+    if (et == 0) FQKV_TRACE_POINT(8);
     if constexpr (GRID) {
       // Whole-row sums: the eight warps' shares, added in warp order.
       for (int m = et; m < p.M; m += kNormThreads) {
@@ -509,6 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (et == 0) FQKV_TRACE_POINT(9);
     // Pass 2: normalise, dtype((h * rstd) * g), over pass 1's rows and chunks; a lane's gain
     // pairs for its kLoadBatch chunks are loaded once and serve all its rows.
     auto load_g2 = [&](int j, uint64_t (&g2)[4]) {
@@ -569,7 +582,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_proxy_async_smem();
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (et == 0) mbar_arrive(normed_bar);
+    // FQKV_FLAG_TEST_WITHHOLD (tests of the failure path): no arrival, so the MMA thread's
+    // bounded wait runs out; it then commits no MMA and the kernel winds down as usual.
+    if (et == 0 && !(p.flags & FQKV_FLAG_TEST_WITHHOLD)) mbar_arrive(normed_bar);
+    if (et == 0) FQKV_TRACE_POINT(10);
 
     if (F8) {
       // e4m3 weights: convert stage s of the ring tile by tile into the conversion slots
@@ -602,6 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     ok = mbar_wait(accum_bar, 0) && ok;
+    if (et == 0) FQKV_TRACE_POINT(13);
     tc_fence_after();
     const int q = warp & 3;             // TMEM lane quadrant this warp may access
     const int half = (warp - 2) >> 2;   // the two warps of a quadrant split the 16-column chunks
@@ -655,6 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile uint32_t* last_flag = tmem_slot + 1;
       if (et == 0) *last_flag = atomicAdd(p.gcnt + grp, 1) == (int)C - 1 ? 1u : 0u;
       asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (et == 0) FQKV_TRACE_POINT(14);
       if (*last_flag) {
         __threadfence();
         const float4* slots4 = reinterpret_cast<const float4*>(p.gpart + (int64_t)grp * C * slot_floats);
@@ -672,6 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (et == 0) p.gcnt[grp] = 0;
       }
+      if (et == 0) FQKV_TRACE_POINT(16);
       cluster_arrive_release_thread();  // the teardown's (one-CTA) cluster barrier
     } else {
       // Cluster epilogue: TMEM -> registers -> this CTA's partial tile in shared memory, laid
@@ -700,6 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
       }
       ok = mbar_wait<true>(part_bar, 0) && ok;
+      if (et == 0) FQKV_TRACE_POINT(14);
       // Lane c of warp 2 sends rank c's share of this CTA's partial tile to slot `rank` of
       // rank c's ring.
       if (warp == 2 && (uint32_t)lane < C && (uint32_t)lane != rank) {
@@ -709,6 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             mapa_shared(smem_u32(recv_bar), o));
       }
       ok = mbar_wait<true>(recv_bar, 0) && ok;
+      if (et == 0) FQKV_TRACE_POINT(15);
       // Every copy into this CTA has landed, so their sources have been read: this thread
       // makes no further access to a peer's shared memory, nor a peer to this CTA's.
       cluster_arrive_release_thread();
@@ -727,6 +748,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         store_quad(f, acc);
       }
+      if (et == 0) FQKV_TRACE_POINT(16);
     }
     (void)ok;
   }
@@ -744,6 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (threadIdx.x == 0) FQKV_TRACE_END();
 }
 
 template <int MPAD, int NT, bool F8, bool GRID = false>

@@ -19,8 +19,10 @@ namespace fqkv {
 // failure; read and cleared by fqkv_device_status().
 extern __device__ int g_status;
 
-// A bounded wait gives up after this many nanoseconds of %globaltimer.
+// A bounded wait gives up after g_wait_limit_ns nanoseconds of %globaltimer: 1 s unless a
+// test shortens it (fqkv_test_set_wait_limit_ns).
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s
+extern __device__ unsigned long long g_wait_limit_ns;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -29,6 +31,65 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 }
 
 __device__ __forceinline__ void record_status(int bits) { atomicOr(&g_status, bits); }
+
+// ------------------------------------------------------------------ timeline trace
+// Profiling builds only (-DFQKV_TRACE): a kernel takes one record per CTA from a buffer
+// installed with fqkv_trace_attach and writes %clock64 at its phase boundaries, plus its
+// block index, SM and %globaltimer at entry and exit, so that CTAs of consecutive launches
+// can be laid out on one time axis.  In the normal build the macros expand to nothing.
+#ifdef FQKV_TRACE
+constexpr int kTraceSlots = 24;
+extern __device__ unsigned long long* g_trace_buf;
+extern __device__ unsigned int g_trace_cap;
+extern __device__ unsigned int g_trace_ctr;
+__device__ __forceinline__ unsigned long long clock64_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+  return t;
+}
+#define FQKV_TRACE_DECL __shared__ unsigned int fqkv_trace_idx_;
+// Thread 0, before the kernel's first block-wide barrier.
+#define FQKV_TRACE_BEGIN()                                                                               \
+  do {                                                                                                   \
+    if (threadIdx.x == 0) {                                                                              \
+      unsigned long long g0;                                                                             \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));                                             \
+      const unsigned long long c0 = ::fqkv::clock64_now();                                               \
+      unsigned int smid;                                                                                 \
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));                                                  \
+      const unsigned int i = ::fqkv::g_trace_buf ? atomicAdd(&::fqkv::g_trace_ctr, 1u) : 0xFFFFFFFFu;   \
+      fqkv_trace_idx_ = i < ::fqkv::g_trace_cap ? i : 0xFFFFFFFFu;                                      \
+      if (fqkv_trace_idx_ != 0xFFFFFFFFu) {                                                              \
+        unsigned long long* r = ::fqkv::g_trace_buf + (size_t)fqkv_trace_idx_ * ::fqkv::kTraceSlots;     \
+        r[0] = (unsigned long long)blockIdx.x | ((unsigned long long)blockIdx.y << 16) |                 \
+               ((unsigned long long)smid << 32) | ((unsigned long long)gridDim.x << 40) |                \
+               ((unsigned long long)gridDim.y << 48);                                                    \
+        r[1] = g0;                                                                                       \
+        r[2] = c0;                                                                                       \
+      }                                                                                                  \
+    }                                                                                                    \
+  } while (0)
+#define FQKV_TRACE_POINT(slot)                                                                           \
+  do {                                                                                                   \
+    if (fqkv_trace_idx_ != 0xFFFFFFFFu)                                                                  \
+      ::fqkv::g_trace_buf[(size_t)fqkv_trace_idx_ * ::fqkv::kTraceSlots + (slot)] = ::fqkv::clock64_now(); \
+  } while (0)
+#define FQKV_TRACE_END()                                                                                 \
+  do {                                                                                                   \
+    if (fqkv_trace_idx_ != 0xFFFFFFFFu) {                                                                \
+      unsigned long long g1;                                                                             \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));                                             \
+      unsigned long long* r = ::fqkv::g_trace_buf + (size_t)fqkv_trace_idx_ * ::fqkv::kTraceSlots;       \
+      r[::fqkv::kTraceSlots - 2] = ::fqkv::clock64_now();                                                        \
+      r[::fqkv::kTraceSlots - 1] = g1;                                                                           \
+    }                                                                                                    \
+  } while (0)
+#else
+#define FQKV_TRACE_DECL
+#define FQKV_TRACE_BEGIN() ((void)0)
+#define FQKV_TRACE_POINT(slot) ((void)0)
+#define FQKV_TRACE_END() ((void)0)
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -106,14 +167,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and records
-// a timeout) if it has not completed within kWaitLimitNs.
+// a timeout) if it has not completed within g_wait_limit_ns.
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long t0 = globaltimer_ns(), limit = *(volatile unsigned long long*)&g_wait_limit_ns;
   for (uint32_t it = 1;; ++it) {
     if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 0u && globaltimer_ns() - t0 > limit) {
       record_status(FQKV_STATUS_WAIT_TIMEOUT);
       return false;
     }
@@ -137,10 +198,10 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // its wake-up delay to every step.  Bounded the same way.
 __device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
   if (mbar_test_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long t0 = globaltimer_ns(), limit = *(volatile unsigned long long*)&g_wait_limit_ns;
   for (uint32_t it = 1;; ++it) {
     if (mbar_test_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 0u && globaltimer_ns() - t0 > limit) {
       record_status(FQKV_STATUS_WAIT_TIMEOUT);
       return false;
     }

@@ -1,5 +1,6 @@
 """Model integrations of the fused RMSNorm + QKV op (the reference's ``integration``
 package, ``integration/__init__.py:1-15``)."""
+from .decode import GraphedGreedyDecoder
 from .llama3_patch import (
     LLAMA3_8B_CONFIG,
     apply_fused_patch,
@@ -9,6 +10,7 @@ from .llama3_patch import (
 )
 
 __all__ = [
+    "GraphedGreedyDecoder",
     "LLAMA3_8B_CONFIG",
     "build_llama3_8b",
     "apply_fused_patch",

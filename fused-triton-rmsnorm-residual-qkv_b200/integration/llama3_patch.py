@@ -26,8 +26,12 @@ other than the last returns its MLP output alone and leaves the updated residual
 in a per-model carry.  The next layer's input call is then
 ``fused_add_rmsnorm_matmul(mlp_out, stream, input_layernorm.weight, [Wq; Wk; Wv])``: one
 launch adds the two (bit-exact), normalises and projects.  The last layer returns the
-full stream, so the final norm is unchanged.  With it, hidden states collected between
-layers (``output_hidden_states``) are the MLP outputs, not the stream.
+full stream, so the final norm is unchanged.  The stream between layers therefore exists
+only inside that carry: ``cross_layer`` is for plain forward passes.  Hidden states
+collected between layers (``output_hidden_states``) and forward hooks on single layers
+see the MLP outputs, not the stream, and a single layer called on its own returns a
+partial value.  The first layer of each forward clears the carry, and a layer that raises
+clears it too.
 
 ``rope=True`` replaces the split / view / transpose / ``apply_rotary_pos_emb`` sequence after
 the fused Q/K/V call by ``qkv_rope_split``: one launch that writes head-major Q, K, V with
@@ -140,7 +144,21 @@ def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None
     h_kv = self._fused_H_kv
     h_q = self._fused_packed_qkv.shape[0] - 2 * h_kv
     carry = getattr(self, "_fused_carry", None)
-    pending = None if carry is None or self._fused_first else carry.pop("stream", None)
+    if carry is not None and self._fused_first:
+        carry.clear()  # a forward that raised part-way leaves nothing behind for this one
+    pending = None if carry is None else carry.pop("stream", None)
+    try:
+        return _patched_body(self, hidden_states, attention_mask, past_key_values, position_embeddings, carry,
+                             pending, lead, attn, h_q, h_kv, **kwargs)
+    except BaseException:
+        if carry is not None:
+            carry.clear()
+        raise
+
+
+def _patched_body(self, hidden_states, attention_mask, past_key_values, position_embeddings, carry, pending, lead,
+                  attn, h_q, h_kv, **kwargs):
+    """The patched layer's work (see _patched_forward)."""
     if pending is None:
         qkv = _fused_op()(hidden_states, None, self.input_layernorm.weight, self._fused_packed_qkv,
                           eps=self.input_layernorm.variance_epsilon)

@@ -17,7 +17,7 @@ from pathlib import Path
 # Constants mirrored from include/fused_rmsnorm_qkv.h.
 F16, BF16, F32 = 0, 1, 2
 SCHED_AUTO, SCHED_SIMT, SCHED_DECODE, SCHED_SPLIT, SCHED_PREFILL, SCHED_GRID = -1, 0, 1, 2, 3, 4
-FLAG_PDL, FLAG_STATIC_WEIGHTS = 1, 2
+FLAG_PDL, FLAG_STATIC_WEIGHTS, FLAG_TEST_WITHHOLD = 1, 2, 4
 ERR_NULL, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_WORKSPACE, ERR_SCHEDULE, ERR_DEVICE, ERR_DEVICE_TIMEOUT, ERR_ALIAS = (
     1, 2, 3, 4, 5, 6, 7, 8, 9)
 STATUS_WAIT_TIMEOUT = 1
@@ -39,6 +39,8 @@ EXPORTED_SYMBOLS = (
     "fqkv_query_schedule",
     "fqkv_last_error",
     "fqkv_device_status",
+    "fqkv_stream_capture_id",
+    "fqkv_test_set_wait_limit_ns",
     "fqkv_version",
 )
 
@@ -80,6 +82,10 @@ def load() -> ctypes.CDLL:
     lib.fqkv_last_error.restype = ctypes.c_char_p
     lib.fqkv_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
     lib.fqkv_device_status.restype = i32
+    lib.fqkv_test_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
+    lib.fqkv_test_set_wait_limit_ns.restype = i32
+    lib.fqkv_stream_capture_id.argtypes = [vp, ctypes.POINTER(ctypes.c_ulonglong)]
+    lib.fqkv_stream_capture_id.restype = i32
     lib.fqkv_version.argtypes = []
     lib.fqkv_version.restype = i32
     lib.fqkv_launch_fp8w.argtypes = [vp, vp, vp, i32, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, f32,
@@ -123,6 +129,19 @@ def rope_split(qkv_ptr, ldq, cos_ptr, sin_ptr, cos_batch, q_ptr, k_ptr, v_ptr, B
                dtype, stream) -> int:
     return load().fqkv_rope_split(qkv_ptr, ldq, cos_ptr, sin_ptr, cos_batch, q_ptr, k_ptr, v_ptr, B, S, n_q, n_kv,
                                   head_dim, dtype, stream)
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Tests of the failure path: the bounded-wait limit of kernels launched from now on
+    (current device); 0 restores the default of 1 s."""
+    check(load().fqkv_test_set_wait_limit_ns(ns), "fqkv_test_set_wait_limit_ns")
+
+
+def stream_capture_id(stream: int) -> int:
+    """Id of the capture active on ``stream``, or 0 when it is not being captured."""
+    cid = ctypes.c_ulonglong(0)
+    check(load().fqkv_stream_capture_id(stream, ctypes.byref(cid)), "fqkv_stream_capture_id")
+    return cid.value
 
 
 def workspace_bytes(M: int, H: int, N: int, dtype: int, schedule: int) -> int:

@@ -32,6 +32,7 @@ streaming the weight before the preceding kernel in the stream has finished.
 """
 from __future__ import annotations
 
+import collections
 import contextlib
 import os
 from typing import Optional, Tuple
@@ -64,10 +65,22 @@ _GRID_AUTO_MAX_M = 2
 _GRID_AUTO_MAX_BYTES = 0.8
 # (M, H, N, dtype, device) -> whether the automatic choice is the grid schedule.
 _grid_choice: dict[tuple, bool] = {}
-# (device, stream) -> zero-filled workspace of the grid schedule.  Its launches leave the
-# arrival counters at zero, and launches on one stream run in order, so one buffer per
-# stream is zeroed once and then reused.
+# Workspaces kept between calls.  Launches on one stream run in order, so calls on a
+# stream can share one buffer:
+#  * (device, stream) -> zero-filled workspace of the grid schedule for eager calls.  Its
+#    launches leave the arrival counters at zero, so the buffer is zeroed once.
+#  * (device, stream, capture id) -> the same for calls made while that stream is being
+#    captured into a CUDA graph.  It is created (zero-filled) inside the capture, so every
+#    replay of that graph zeroes it before its first grid launch, and no other graph and no
+#    eager call uses it: graphs replayed at the same time on different streams do not share
+#    counters.  The newest _CAPTURE_KEEP captures keep theirs.
+#  * (device, stream) -> workspace of the pre-pass schedules (split, prefill) for eager
+#    calls; nothing in it needs to start at zero.  Calls made during a capture allocate
+#    theirs from the graph's private pool instead.
 _grid_ws: dict[tuple[int, int], torch.Tensor] = {}
+_grid_ws_capture: "collections.OrderedDict[tuple[int, int, int], torch.Tensor]" = collections.OrderedDict()
+_CAPTURE_KEEP = 16
+_prepass_ws: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _env_flag(name: str) -> bool:
@@ -143,11 +156,33 @@ def _tma_ready(H: int, tensors, strides) -> bool:
 
 
 def _grid_workspace(index: int, stream: int, nbytes: int, dev: torch.device) -> torch.Tensor:
-    """The zero-filled grid-schedule workspace of this device and stream, grown as needed."""
+    """The zero-filled grid-schedule workspace of this device and stream (and of the capture
+    running on it, if any), grown as needed."""
+    if torch.cuda.is_current_stream_capturing():
+        key = (index, stream, _lib.stream_capture_id(stream))
+        buf = _grid_ws_capture.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)  # a memset node of this graph
+            _grid_ws_capture[key] = buf
+            while len(_grid_ws_capture) > _CAPTURE_KEEP:
+                _grid_ws_capture.popitem(last=False)
+        return buf
     buf = _grid_ws.get((index, stream))
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         _grid_ws[(index, stream)] = buf
+    return buf
+
+
+def _prepass_workspace(index: int, stream: int, nbytes: int, dev: torch.device) -> torch.Tensor:
+    """Workspace of the pre-pass schedules: one buffer per device and stream for eager calls,
+    grown as needed; a fresh one from the graph's pool while the stream is captured."""
+    if torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    buf = _prepass_ws.get((index, stream))
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _prepass_ws[(index, stream)] = buf
     return buf
 
 
@@ -212,7 +247,7 @@ def _call(x2, r2, g, gcode, w, out2, rout2, M, H, N, ldx, ldr, ldw, ldo, ldro, e
     if code == _lib.SCHED_GRID:
         ws = _grid_workspace(index, stream, ws_bytes, x2.device)
     else:
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes > 0 else None
+        ws = _prepass_workspace(index, stream, ws_bytes, x2.device) if ws_bytes > 0 else None
     return _lib.launch(
         x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), gcode, w.data_ptr(),
         out2.data_ptr(), rout2.data_ptr() if rout2 is not None else None, M, H, N, ldx, ldr, ldw, ldo, ldro,

@@ -73,6 +73,14 @@ extern "C" {
 #define FQKV_FLAG_STATIC_WEIGHTS 2  /* `weight` is not written by the preceding grid in the
                                        stream: the decode kernel may start streaming it
                                        before that grid has finished (only with FLAG_PDL) */
+#define FQKV_FLAG_TEST_WITHHOLD  4  /* tests of the failure path only (decode and grid
+                                       schedules): the kernel's norm warps withhold their
+                                       arrival on the barrier the MMA thread waits for, so that
+                                       wait runs out (after the limit set by
+                                       fqkv_test_set_wait_limit_ns), FQKV_STATUS_WAIT_TIMEOUT is
+                                       recorded and the kernel winds down and returns.  `out`
+                                       is undefined after such a launch; residual_out is
+                                       written as usual. */
 
 /* Error codes (> 0). */
 #define FQKV_ERR_NULL        1  /* a required pointer is NULL                                */
@@ -142,10 +150,23 @@ FQKV_API const char* fqkv_last_error(void);
  * current device.  *status receives FQKV_STATUS_* bits. */
 FQKV_API int fqkv_device_status(void* stream, int* status);
 
+/* Tests of the failure path only: the time after which every bounded wait of the
+ * library's kernels on the current device gives up, in nanoseconds of %globaltimer
+ * (0 restores the default, 1 s).  Applies to kernels launched after the call.  No
+ * counterpart in the reference (its Triton kernels have no waits). */
+FQKV_API int fqkv_test_set_wait_limit_ns(unsigned long long ns);
+
+/* *id receives the id of the stream capture active on `stream` (cudaStreamGetCaptureInfo),
+ * or 0 when the stream is not being captured.  A host wrapper keeps scratch that must be
+ * zero before its first use (the GRID schedule's counters) per capture with it: a buffer
+ * zeroed inside one capture is zeroed by every replay of that graph, and by nothing else.
+ * No counterpart in the reference (Triton launches need no scratch). */
+FQKV_API int fqkv_stream_capture_id(void* stream, unsigned long long* id);
+
 /*
  * The op without a workspace, for callers that cannot allocate device memory when they
  * run it -- an inference engine's plugin whose enqueue step must not allocate, a runtime
- * with a fixed memory budget, code running while a stream is being captured.  No
+ * with a fixed memory budget that allocates nothing after start-up.  No
  * counterpart in the reference (its Triton kernels need no scratch).
  * Runs the SPLIT schedule (norm pre-pass + stream-K GEMM) on a fixed device array owned
  * by the library (about 5.5 MB on every GPU that loads the library, held until exit), so

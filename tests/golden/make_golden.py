@@ -40,7 +40,7 @@ def load_reference_baseline(ref_root: Path):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of a checkout of the reference repository")
     ap.add_argument("--out", default=str(Path(__file__).resolve().parent / "golden.npz"))
     a = ap.parse_args()
     ref_fn = load_reference_baseline(Path(a.reference))

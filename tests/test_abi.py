@@ -69,6 +69,11 @@ SPACED = dict(x=1 << 32, r=2 << 32, g=3 << 32, w=4 << 32, out=5 << 32)
     (dict(M=1 << 31), _lib.ERR_SHAPE),
     (dict(schedule=9), _lib.ERR_SCHEDULE),
     (dict(flags=64), _lib.ERR_SCHEDULE),
+    # the failure-path test flag is for the fused decode kernels only
+    (dict(schedule=_lib.SCHED_SPLIT, flags=_lib.FLAG_TEST_WITHHOLD), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_PREFILL, M=4096, flags=_lib.FLAG_TEST_WITHHOLD), _lib.ERR_SCHEDULE),
+    (dict(schedule=_lib.SCHED_SIMT, flags=_lib.FLAG_TEST_WITHHOLD), _lib.ERR_SCHEDULE),
+    (dict(H=260, ldx=260, ldr=260, ldw=260, flags=_lib.FLAG_TEST_WITHHOLD), _lib.ERR_SCHEDULE),
     (dict(schedule=_lib.SCHED_DECODE, M=65), _lib.ERR_SCHEDULE),
     (dict(schedule=_lib.SCHED_SPLIT, M=129), _lib.ERR_SCHEDULE),
     (dict(schedule=_lib.SCHED_GRID, M=9), _lib.ERR_SCHEDULE),
@@ -173,6 +178,7 @@ def fp8_call(**kw):
 @pytest.mark.parametrize("kw,code", [
     (dict(w=None), _lib.ERR_NULL),
     (dict(sc=None), _lib.ERR_NULL),
+    (dict(flags=_lib.FLAG_TEST_WITHHOLD), _lib.ERR_SCHEDULE),
     (dict(x=None), _lib.ERR_NULL),
     (dict(dtype=_lib.F32), _lib.ERR_DTYPE),
     (dict(M=65), _lib.ERR_SCHEDULE),          # decode sizes only
@@ -187,10 +193,15 @@ def test_fp8w_rejects_before_any_cuda_call(kw, code):
 
 
 def test_profile_case_parses_its_arguments():
-    """The profiler workload module takes its shape and schedule from the command line
-    (no GPU needed to print its usage)."""
-    from triton_fused_rmsnorm_qkv import profile_case
+    """The profiler workload (``bench.py --profile-case``) takes its shape and schedule from
+    the command line (no GPU needed to print its usage)."""
+    import subprocess
+    import sys
+    from pathlib import Path
 
-    with pytest.raises(SystemExit) as e:
-        profile_case.main(["--help"])
-    assert e.value.code == 0
+    root = Path(__file__).resolve().parents[1]
+    res = subprocess.run([sys.executable, str(root / "bench.py"), "--help"], capture_output=True, text=True,
+                         timeout=300)
+    assert res.returncode == 0, res.stderr
+    for opt in ("--profile-case", "--H", "--N", "--schedule", "--fp8w", "--calls"):
+        assert opt in res.stdout

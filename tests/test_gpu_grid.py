@@ -140,3 +140,40 @@ def test_automatic_choice():
         assert llama["schedule"] == "decode"
     run_grid(4, 3584, 4608, seed=762, schedule=None)
     assert get_autotune_best_config(4, 3584)["schedule"] == "decode"
+
+
+def test_automatic_grid_under_graph_capture():
+    """The grid schedule chosen automatically inside CUDA graph captures: each capture keeps
+    its own zero-filled counters (zeroed by its own replays), so two graphs captured on the
+    same stream, replayed in reverse order, and an eager call afterwards all match the oracle
+    and leave their counters at zero."""
+    M, H, N, eps = 1, 3584, 4608, 1e-6
+    assert fk.schedule_info(M, H, N)["schedule"] == _lib.SCHED_GRID
+    cases = [make_case(M, H, N, torch.bfloat16, seed=900 + i) for i in range(3)]
+    dev = [tuple(t.cuda() for t in c) for c in cases]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graphs, outs = [], []
+    with torch.cuda.stream(side):
+        for i in range(2):
+            x, r, g, w = dev[i]
+            fused_add_rmsnorm_matmul(x[None], r[None], g, w, eps)  # warm-up outside the capture
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=side):
+                outs.append(fused_add_rmsnorm_matmul(x[None], r[None], g, w, eps))
+            graphs.append(gr)
+    torch.cuda.synchronize()
+    for i in (1, 0):
+        for o in outs[i]:
+            o.zero_()
+        graphs[i].replay()
+        torch.cuda.synchronize()
+        check(outs[i][0][0].cpu(), outs[i][1][0].cpu(), *cases[i], eps)
+    x, r, g, w = dev[2]
+    out, hidden = fused_add_rmsnorm_matmul(x[None], r[None], g, w, eps)
+    torch.cuda.synchronize()
+    check(out[0].cpu(), hidden[0].cpu(), *cases[2], eps)
+    assert counters_zero()
+    assert all(int(buf[:4096].count_nonzero()) == 0 for buf in fk._grid_ws_capture.values())
+    assert device_status() == 0
+    del graphs

@@ -153,3 +153,35 @@ def test_patched_llama3_8b_two_layers_decode_and_prefill(mode):
         assert rel < 3e-2, float(rel)
     del model
     torch.cuda.empty_cache()
+
+
+def test_cross_layer_carry_is_cleared_on_first_layer_and_on_error(monkeypatch):
+    """The cross-layer carry holds the residual stream between layers: the first layer of a
+    forward starts from an empty carry, and a layer that raises leaves it empty."""
+    from integration import llama3_patch
+
+    model = tiny_llama()
+    apply_fused_patch(model, cross_layer=True)
+    first, second = model.model.layers[0], model.model.layers[1]
+    carry = first._fused_carry
+    assert carry is second._fused_carry
+
+    seen = {}
+
+    def fake_body(self, hidden_states, attention_mask, past_key_values, position_embeddings, carry_, pending, *a,
+                  **kw):
+        seen["pending"] = pending
+        if self is second:
+            raise RuntimeError("boom")
+        return hidden_states
+
+    monkeypatch.setattr(llama3_patch, "_patched_body", fake_body)
+    h = torch.zeros(1, 1, 256)
+    carry["stream"] = "stale"
+    first(h, position_embeddings=(None, None))
+    assert seen["pending"] is None and "stream" not in carry   # stale entry dropped by the first layer
+    carry["stream"] = "from layer 0"
+    with pytest.raises(RuntimeError):
+        second(h, position_embeddings=(None, None))
+    assert seen["pending"] == "from layer 0" and carry == {}
+    remove_fused_patch(model)

@@ -1,12 +1,14 @@
 """fqkv_launch_noalloc: the op for callers that cannot allocate device memory when they
-run it (an engine plugin whose enqueue must not allocate, a fixed-budget runtime, code
-running under stream capture).  It runs the split schedule on a fixed device array owned
-by the library instead of a caller workspace.
+run it -- an inference engine's plugin whose enqueue step must not allocate (the engine
+owns all device memory, and cudaMalloc can synchronise the device), or a runtime with a
+fixed memory budget that allocates nothing after start-up.  It runs the split schedule on
+a fixed device array owned by the library instead of a caller workspace.
 
-Its output must match the regular entry point's on the same inputs -- same tolerance as
-the other parity tests -- on two calls in a row (the second call reuses the array the
-first one left behind).  This file is collected last so that a failure here comes after
-every other test has run.
+Each call's output is checked against the regular entry point's on the same inputs and
+against the CPU oracle, with the tolerance of the other parity tests, on calls in a row:
+the later calls reuse the array the earlier ones left behind, one of them with the same
+shape as the first.  This file is collected last so that a failure here comes after every
+other test has run.
 """
 from __future__ import annotations
 
@@ -15,7 +17,7 @@ import ctypes
 import pytest
 import torch
 
-from oracle import make_case, parity_metrics, within_bars
+from oracle import forward, make_case, parity_metrics, within_bars
 from triton_fused_rmsnorm_qkv import _lib, fused_add_rmsnorm_matmul
 
 pytestmark = pytest.mark.gpu
@@ -39,19 +41,24 @@ def _noalloc(x, r, g, w, eps):
     return rc, out, hidden
 
 
-def test_noalloc_matches_regular_entry_point_on_two_calls():
-    cases = [(16, 4096, 6144, torch.bfloat16, True, 1e-5), (7, 1024, 1280, torch.float16, False, 1e-6)]
-    for call, (M, H, N, dtype, res, eps) in enumerate(cases):
-        x, r, g, w = (t.cuda() if t is not None else None for t in make_case(M, H, N, dtype, seed=50 + call,
-                                                                             has_residual=res))
+def test_noalloc_matches_regular_entry_point_on_calls_in_a_row():
+    cases = [(16, 4096, 6144, torch.bfloat16, True, 1e-5, 50), (7, 1024, 1280, torch.float16, False, 1e-6, 51),
+             (16, 4096, 6144, torch.bfloat16, True, 1e-5, 52)]  # the first shape again, new inputs
+    for call, (M, H, N, dtype, res, eps, seed) in enumerate(cases):
+        xc, rc_, gc, wc = make_case(M, H, N, dtype, seed=seed, has_residual=res)
+        x, r, g, w = (t.cuda() if t is not None else None for t in (xc, rc_, gc, wc))
         rc, out, hidden = _noalloc(x, r, g, w, eps)
         assert rc == 0, _lib.last_error()
         ref_out, ref_hidden = fused_add_rmsnorm_matmul(x[None], r[None] if r is not None else None, g, w, eps,
                                                       schedule="split")
         torch.cuda.synchronize()
         m = parity_metrics(out.cpu(), ref_out[0].cpu())
-        assert within_bars(m), (call, m)
+        assert within_bars(m), (call, "vs fqkv_launch", m)
         assert torch.equal(hidden.cpu(), ref_hidden[0].cpu()), call
+        oracle_out, oracle_hidden = forward(xc, rc_, gc, wc, eps)
+        m = parity_metrics(out.cpu(), oracle_out)
+        assert within_bars(m), (call, "vs oracle", m)
+        assert torch.equal(hidden.cpu(), oracle_hidden), call
 
 
 def test_noalloc_rejects_sizes_beyond_its_array():
