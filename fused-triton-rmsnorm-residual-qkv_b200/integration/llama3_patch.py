@@ -33,9 +33,10 @@ see the MLP outputs, not the stream, and a single layer called on its own return
 partial value.  The first layer of each forward clears the carry, and a layer that raises
 clears it too.
 
-``rope=True`` replaces the split / view / transpose / ``apply_rotary_pos_emb`` sequence after
-the fused Q/K/V call by ``qkv_rope_split``: one launch that writes head-major Q, K, V with
-Q and K rotated, bit-identical to that sequence.
+``rope=True`` replaces the fused Q/K/V call and the split / view / transpose /
+``apply_rotary_pos_emb`` sequence after it by ``fused_add_rmsnorm_qkv_rope``: at decode sizes
+one launch whose epilogue writes head-major Q, K, V with Q and K rotated, bit-identical to
+that sequence (other sizes: the fused call and ``qkv_rope_split``).
 
 Written against transformers 5.5 (``LlamaDecoderLayer.forward`` / ``LlamaAttention``).
 """
@@ -56,6 +57,7 @@ from transformers.models.llama.modeling_llama import (
 
 from triton_fused_rmsnorm_qkv import (
     fused_add_rmsnorm_matmul,
+    fused_add_rmsnorm_qkv_rope,
     fused_rmsnorm_residual_matmul,
     fused_rmsnorm_residual_matmul_fixed,
     qkv_rope_split,
@@ -159,14 +161,27 @@ def _patched_forward(self, hidden_states, attention_mask=None, position_ids=None
 def _patched_body(self, hidden_states, attention_mask, past_key_values, position_embeddings, carry, pending, lead,
                   attn, h_q, h_kv, **kwargs):
     """The patched layer's work (see _patched_forward)."""
+    cos, sin = position_embeddings
+    ln = self.input_layernorm
+    if getattr(self, "_fused_rope", False) and not _fixed():
+        # One launch: norm, projection, head split and rotary embedding (decode sizes; the
+        # op runs the projection and the split as two launches otherwise).
+        heads = (h_q // attn.head_dim, h_kv // attn.head_dim, attn.head_dim)
+        if pending is None:
+            q, k, v = fused_add_rmsnorm_qkv_rope(hidden_states, None, ln.weight, self._fused_packed_qkv, cos, sin,
+                                                 *heads, ln.variance_epsilon, return_residual=False)
+        else:
+            q, k, v, hidden_states = fused_add_rmsnorm_qkv_rope(hidden_states, pending, ln.weight,
+                                                                self._fused_packed_qkv, cos, sin, *heads,
+                                                                ln.variance_epsilon)
+        return _attend_and_mlp(self, hidden_states, q, k, v, attention_mask, past_key_values, carry, lead, attn,
+                               **kwargs)
     if pending is None:
-        qkv = _fused_op()(hidden_states, None, self.input_layernorm.weight, self._fused_packed_qkv,
-                          eps=self.input_layernorm.variance_epsilon)
+        qkv = _fused_op()(hidden_states, None, ln.weight, self._fused_packed_qkv, eps=ln.variance_epsilon)
     else:
         # The previous layer's MLP output arrives with the stream it belongs to.
-        qkv, hidden_states = _fused_add(hidden_states, pending, self.input_layernorm.weight, self._fused_packed_qkv,
-                                        self.input_layernorm.variance_epsilon)
-    cos, sin = position_embeddings
+        qkv, hidden_states = _fused_add(hidden_states, pending, ln.weight, self._fused_packed_qkv,
+                                        ln.variance_epsilon)
     if getattr(self, "_fused_rope", False):
         q, k, v = qkv_rope_split(qkv, cos, sin, h_q // attn.head_dim, h_kv // attn.head_dim, attn.head_dim)
     else:
@@ -175,6 +190,11 @@ def _patched_body(self, hidden_states, attention_mask, past_key_values, position
         k = k.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
         v = v.reshape(*lead, -1, attn.head_dim).transpose(1, 2)
         q, k = apply_rotary_pos_emb(q, k, cos, sin)
+    return _attend_and_mlp(self, hidden_states, q, k, v, attention_mask, past_key_values, carry, lead, attn, **kwargs)
+
+
+def _attend_and_mlp(self, hidden_states, q, k, v, attention_mask, past_key_values, carry, lead, attn, **kwargs):
+    """The rest of the layer after Q/K/V: KV cache, attention, o_proj, residual, MLP."""
     if past_key_values is not None:
         k, v = past_key_values.update(k, v, attn.layer_idx)
     attend = ALL_ATTENTION_FUNCTIONS.get_interface(attn.config._attn_implementation, eager_attention_forward)

@@ -20,6 +20,7 @@ from .kernel import (
     fused_rmsnorm_residual_qkv_fixed,
     get_autotune_best_config,
     qkv_rope_split,
+    fused_add_rmsnorm_qkv_rope,
     quantize_weight_e4m3,
     schedule_info,
 )
@@ -34,6 +35,7 @@ __all__ = [
     "fused_add_rmsnorm_matmul",
     "device_status",
     "qkv_rope_split",
+    "fused_add_rmsnorm_qkv_rope",
     "fused_add_rmsnorm_matmul_fp8w",
     "quantize_weight_e4m3",
     "schedule_info",

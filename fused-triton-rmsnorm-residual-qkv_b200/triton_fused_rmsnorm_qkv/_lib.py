@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "fqkv_launch_noalloc",
     "fqkv_launch_fp8w",
     "fqkv_rope_split",
+    "fqkv_launch_rope",
     "fqkv_workspace_bytes",
     "fqkv_query_schedule",
     "fqkv_last_error",
@@ -93,6 +94,9 @@ def load() -> ctypes.CDLL:
     lib.fqkv_launch_fp8w.restype = i32
     lib.fqkv_rope_split.argtypes = [vp, i64, vp, vp, i64, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp]
     lib.fqkv_rope_split.restype = i32
+    lib.fqkv_launch_rope.argtypes = [vp, vp, vp, i32, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp, vp,
+                                     i64, i32, i32, i32, f32, i32, i32, vp]
+    lib.fqkv_launch_rope.restype = i32
     _lib = lib
     return lib
 
@@ -142,6 +146,13 @@ def stream_capture_id(stream: int) -> int:
     cid = ctypes.c_ulonglong(0)
     check(load().fqkv_stream_capture_id(stream, ctypes.byref(cid)), "fqkv_stream_capture_id")
     return cid.value
+
+
+def launch_rope(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, q_ptr, k_ptr, v_ptr, rout_ptr, B, S, H, ldx, ldr, ldw, ldro,
+                cos_ptr, sin_ptr, cos_batch, n_q, n_kv, head_dim, eps, dtype, flags, stream) -> int:
+    return load().fqkv_launch_rope(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, q_ptr, k_ptr, v_ptr, rout_ptr, B, S, H, ldx,
+                                   ldr, ldw, ldro, cos_ptr, sin_ptr, cos_batch, n_q, n_kv, head_dim,
+                                   ctypes.c_float(eps), dtype, flags, stream)
 
 
 def workspace_bytes(M: int, H: int, N: int, dtype: int, schedule: int) -> int:

@@ -489,6 +489,98 @@ def qkv_rope_split(
     return q, k, v
 
 
+def _rope_tables(cos: torch.Tensor, sin: torch.Tensor, B: int, S: int, head_dim: int, like: torch.Tensor):
+    """cos / sin as contiguous (1 or B, S, head_dim) tensors of ``like``'s dtype and device."""
+    tabs = []
+    for name, t in (("cos", cos), ("sin", sin)):
+        if t.dtype != like.dtype or t.device != like.device:
+            raise TypeError(f"{name} must have the activations' dtype and device ({like.dtype}, {like.device})")
+        if t.dim() == 2:
+            t = t.unsqueeze(0)
+        if t.dim() != 3 or t.shape[1:] != (S, head_dim) or t.shape[0] not in (1, B):
+            raise ValueError(f"{name} must be (B, S, d), (1, S, d) or (S, d); got {tuple(t.shape)}")
+        tabs.append(t.contiguous())
+    if tabs[0].shape[0] != tabs[1].shape[0]:
+        raise ValueError("cos and sin must have the same batch size")
+    return tabs
+
+
+def fused_add_rmsnorm_qkv_rope(
+    x: torch.Tensor,
+    residual: Optional[torch.Tensor],
+    rms_weight: torch.Tensor,
+    qkv_weight: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    n_q_heads: int,
+    n_kv_heads: int,
+    head_dim: Optional[int] = None,
+    eps: float = 1e-6,
+    *,
+    return_residual: bool = True,
+    static_weights: Optional[bool] = None,
+):
+    """Residual add + RMSNorm + packed Q/K/V projection + head split + rotary embedding.
+
+    Returns ``(q, k, v, hidden)`` (or ``(q, k, v)`` when ``return_residual`` is False):
+    ``q`` (B, n_q, S, d), ``k`` and ``v`` (B, n_kv, S, d), contiguous, Q and K rotated by
+    ``x * cos + rotate_half(x) * sin`` -- bit-identical to ``fused_add_rmsnorm_matmul``
+    followed by ``qkv_rope_split`` (the sequence of llama3_patch.py:148-168).  Decode sizes
+    (B * S <= 32, head_dim 64 or 128) run as one launch, the rotary split in the projection's
+    epilogue; other sizes run the two launches.
+    """
+    assert x.is_cuda, "Fused kernel requires CUDA tensors"
+    B, S, H = x.shape
+    N = qkv_weight.shape[0]
+    assert qkv_weight.shape[1] == H, f"weight must be (N_OUT, H); got {qkv_weight.shape} for H={H}"
+    heads = n_q_heads + 2 * n_kv_heads
+    if head_dim is None:
+        head_dim = N // heads
+    if heads * head_dim != N:
+        raise ValueError(f"weight rows {N} are not ({n_q_heads} + 2 * {n_kv_heads}) * {head_dim}")
+    dt = _DTYPE_CODE.get(x.dtype)
+    if dt is None:
+        raise TypeError(f"x must be float16 or bfloat16, got {x.dtype}")
+    M = B * S
+    hidden = torch.empty_like(x) if return_residual else None
+    tabs = _rope_tables(cos, sin, B, S, head_dim, x)
+    if static_weights is None:
+        static_weights = _env_flag("FQKV_STATIC_WEIGHTS")
+    x2 = _rows(x, M, H)
+    r2 = _rows(residual, M, H) if residual is not None else None
+    w = qkv_weight if qkv_weight.stride(1) == 1 else qkv_weight.contiguous()
+    g = rms_weight.reshape(H)
+    if g.stride(0) != 1:
+        g = g.contiguous()
+    gcode = _GAIN_CODE.get(g.dtype)
+    tensors = [t for t in (x2, r2, g, w, hidden, *tabs) if t is not None]
+    strides = [_row_stride(x2), w.stride(0)] + ([_row_stride(r2)] if r2 is not None else [])
+    one_launch = (M <= 32 and head_dim in (64, 128) and gcode is not None and w.dtype == x.dtype
+                  and (r2 is None or r2.dtype == x.dtype) and _tma_ready(H, tensors, strides))
+    if one_launch:
+        q = torch.empty(B, n_q_heads, S, head_dim, dtype=x.dtype, device=x.device)
+        k = torch.empty(B, n_kv_heads, S, head_dim, dtype=x.dtype, device=x.device)
+        v = torch.empty_like(k)
+        rout2 = _rows(hidden, M, H) if hidden is not None else None
+        flags = _lib.FLAG_PDL | (_lib.FLAG_STATIC_WEIGHTS if static_weights else 0)
+        dev = x.device
+        ctx = contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
+        with ctx:
+            rc = _lib.launch_rope(
+                x2.data_ptr(), r2.data_ptr() if r2 is not None else None, g.data_ptr(), gcode, w.data_ptr(),
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), rout2.data_ptr() if rout2 is not None else None, B, S, H,
+                _row_stride(x2), _row_stride(r2) if r2 is not None else 0, w.stride(0),
+                _row_stride(rout2) if rout2 is not None else 0, tabs[0].data_ptr(), tabs[1].data_ptr(),
+                tabs[0].shape[0], n_q_heads, n_kv_heads, head_dim, float(eps), dt, flags, _current_stream(dev.index))
+        if rc != _lib.ERR_SCHEDULE:  # no configuration fits this device: the two launches below
+            _lib.check(rc, "fqkv_launch_rope")
+            return (q, k, v, hidden) if return_residual else (q, k, v)
+    out = _fused(x, residual, rms_weight, qkv_weight, eps, residual_out=hidden, schedule=None,
+                 static_weights=static_weights)
+    q, k, v = qkv_rope_split(out, tabs[0], tabs[1], n_q_heads, n_kv_heads, head_dim)
+    return (q, k, v, hidden) if return_residual else (q, k, v)
+
+
 def fused_rmsnorm_residual_matmul_fixed(
     x: torch.Tensor,
     residual: Optional[torch.Tensor],

@@ -143,6 +143,27 @@ FQKV_API int64_t fqkv_workspace_bytes(int64_t M, int64_t H, int64_t N, int dtype
 FQKV_API int fqkv_query_schedule(int64_t M, int64_t H, int64_t N, int dtype, int schedule,
                         fqkv_schedule_info* info);
 
+/*
+ * The op with the Q/K/V split and the rotary position embedding in the projection's
+ * epilogue: one launch that writes head-major Q, K, V (Q and K rotated) and the updated
+ * residual, bit-identical to fqkv_launch followed by fqkv_rope_split.  Replaces the fused
+ * call plus the split / view / transpose / apply_rotary_pos_emb sequence of the reference's
+ * Llama integration (llama3_patch.py:148-168).  No counterpart in the reference's C surface.
+ *   x, residual, rms_weight, weight, residual_out, ld*, eps, dtype, flags: as fqkv_launch,
+ *                with M = B * S tokens (row m = b * S + s) and N = (n_q + 2 n_kv) * head_dim
+ *   q     [B, n_q, S, head_dim]   k, v  [B, n_kv, S, head_dim]   dtype, contiguous
+ *   cos, sin  [cos_batch, S, head_dim] dtype, contiguous; cos_batch is 1 (shared) or B
+ * Decode sizes only: M <= 32, head_dim 64 or 128, and a configuration of the pipelined
+ * decode kernel that fits the device; otherwise FQKV_ERR_SCHEDULE (run fqkv_launch and
+ * fqkv_rope_split).  All tensors 16-byte aligned.  Needs no workspace.
+ */
+FQKV_API int fqkv_launch_rope(const void* x, const void* residual, const void* rms_weight,
+                int rms_weight_dtype, const void* weight, void* q, void* k, void* v, void* residual_out,
+                int64_t B, int64_t S, int64_t H, int64_t ldx, int64_t ldr, int64_t ldw, int64_t ldro,
+                const void* cos, const void* sin, int64_t cos_batch,
+                int n_q_heads, int n_kv_heads, int head_dim,
+                float eps, int dtype, int flags, void* stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 FQKV_API const char* fqkv_last_error(void);
 

@@ -205,3 +205,30 @@ def test_profile_case_parses_its_arguments():
     assert res.returncode == 0, res.stderr
     for opt in ("--profile-case", "--H", "--N", "--schedule", "--fp8w", "--calls"):
         assert opt in res.stdout
+
+
+def fused_rope_call(**kw):
+    a = dict(x=1 << 32, r=2 << 32, g=3 << 32, gdt=_lib.BF16, w=4 << 32, q=5 << 32, k=6 << 32, v=7 << 32,
+             rout=None, B=1, S=1, H=4096, ldx=4096, ldr=4096, ldw=4096, ldro=4096, cos=8 << 32, sin=9 << 32,
+             cb=1, n_q=32, n_kv=8, d=128, eps=1e-5, dtype=_lib.BF16, flags=0, stream=None)
+    a.update(kw)
+    return _lib.launch_rope(a["x"], a["r"], a["g"], a["gdt"], a["w"], a["q"], a["k"], a["v"], a["rout"], a["B"],
+                            a["S"], a["H"], a["ldx"], a["ldr"], a["ldw"], a["ldro"], a["cos"], a["sin"], a["cb"],
+                            a["n_q"], a["n_kv"], a["d"], a["eps"], a["dtype"], a["flags"], a["stream"])
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=None), _lib.ERR_NULL),
+    (dict(cos=None), _lib.ERR_NULL),
+    (dict(dtype=_lib.F32), _lib.ERR_DTYPE),
+    (dict(d=96), _lib.ERR_SHAPE),                     # the epilogue takes head_dim 64 or 128
+    (dict(cb=3, B=2), _lib.ERR_SHAPE),                # cos rows neither 1 nor B
+    (dict(B=33), _lib.ERR_SCHEDULE),                  # more tokens than the decode epilogue takes
+    (dict(flags=_lib.FLAG_TEST_WITHHOLD), _lib.ERR_SCHEDULE),
+    (dict(ldw=4000), _lib.ERR_SHAPE),
+    (dict(q=(1 << 32) + 256), _lib.ERR_ALIAS),        # q inside x
+    (dict(k=(5 << 32) + 256), _lib.ERR_ALIAS),        # k inside q
+    (dict(cos=(8 << 32) + 2), _lib.ERR_ALIGN),
+])
+def test_fused_rope_rejects_before_any_cuda_call(kw, code):
+    assert fused_rope_call(**kw) == code, _lib.last_error()
