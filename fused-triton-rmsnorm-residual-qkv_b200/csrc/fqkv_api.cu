@@ -7,7 +7,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
-#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -174,17 +173,6 @@ bool tma_eligible(const Problem& p) {
 
 int auto_schedule_for(int64_t M, int64_t H, int64_t N, const DeviceInfo* dev);
 
-// The decode schedule runs the pipelined kernel (fqkv_decode_pipe.cu) for M <= 32 when one
-// of its configurations fits the device, else the cluster kernel of fqkv_decode.cu.
-// FQKV_DECODE_KERNEL=cluster forces the latter (comparisons).
-bool use_pipe(int M, int H, int N, int sms, PipeConfig* pc) {
-  static const bool off = [] {
-    const char* v = std::getenv("FQKV_DECODE_KERNEL");
-    return v && std::strcmp(v, "cluster") == 0;
-  }();
-  return !off && M <= kPipeMaxM && pipe_pick_config(M, H, N, sms, pc) == 0;
-}
-
 // The current device's description, or nullptr (recording no error) when there is none.
 const DeviceInfo* current_device_or_null(DeviceInfo* buf) {
   const std::string saved = t_last_error;
@@ -222,9 +210,7 @@ int auto_schedule_for(int64_t M, int64_t H, int64_t N, const DeviceInfo* dev) {
   if (H % 8 || H > kPrepassMaxH) return FQKV_SCHED_SIMT;
   if (M > kDecodeMaxM) return FQKV_SCHED_PREFILL;
   DecodeConfig c;
-  PipeConfig pc;
-  if (!dev || dev->major != 10 || use_pipe((int)M, (int)H, (int)N, dev->sms, &pc) ||
-      decode_pick_config((int)M, (int)H, (int)N, dev->sms, &c) == 0)
+  if (!dev || dev->major != 10 || decode_pick_config((int)M, (int)H, (int)N, dev->sms, &c) == 0)
     return FQKV_SCHED_DECODE;
   return FQKV_SCHED_SPLIT;
 }
@@ -420,10 +406,11 @@ extern "C" FQKV_API int fqkv_rope_split(const void* qkv, int64_t ldq, const void
   return e == cudaSuccess ? 0 : cuda_fail(e, "rope split kernel launch");
 }
 
-// The op with the Q/K/V split and the rotary embedding in its epilogue: the pipelined decode
-// kernel's tile owners write head-major Q, K, V (Q and K rotated) instead of the packed
-// output.  Replaces fqkv_launch followed by fqkv_rope_split (the llama3_patch.py:148-168
-// sequence) with one launch, bit-identical to the two.
+// The op with the Q/K/V split and the rotary embedding in its epilogue: each CTA of the
+// fused decode kernel reduces whole 128-row blocks of the output and writes them head-major
+// (Q and K rotated) instead of the packed output.  Replaces fqkv_launch followed by
+// fqkv_rope_split (the llama3_patch.py:148-168 sequence) with one launch, bit-identical to
+// the two.
 extern "C" FQKV_API int fqkv_launch_rope(const void* x, const void* residual, const void* rms_weight,
                                          int rms_weight_dtype, const void* weight, void* q, void* k, void* v,
                                          void* residual_out, int64_t B, int64_t S, int64_t H, int64_t ldx,
@@ -446,9 +433,9 @@ extern "C" FQKV_API int fqkv_launch_rope(const void* x, const void* residual, co
   if (flags & ~(FQKV_FLAG_PDL | FQKV_FLAG_STATIC_WEIGHTS))
     return fail(FQKV_ERR_SCHEDULE, "unknown flag bits 0x%x", flags);
   const int64_t M = B * S, N = (int64_t)(n_q_heads + 2 * n_kv_heads) * head_dim;
-  if (M > kPipeMaxM)
+  if (M > kDecodeRopeMaxM)
     return fail(FQKV_ERR_SCHEDULE, "the fused rotary epilogue takes at most %d tokens (M = %lld); use fqkv_launch "
-                "and fqkv_rope_split", kPipeMaxM, (long long)M);
+                "and fqkv_rope_split", kDecodeRopeMaxM, (long long)M);
   if (H > INT32_MAX || N > INT32_MAX) return fail(FQKV_ERR_SHAPE, "H and N must be below 2^31");
   if (ldx < H || ldw < H || (residual && ldr < H) || (residual_out && ldro < H))
     return fail(FQKV_ERR_SHAPE, "a row stride is smaller than its row length");
@@ -476,41 +463,29 @@ extern "C" FQKV_API int fqkv_launch_rope(const void* x, const void* residual, co
   DeviceInfo d;
   if (int rc = device_info(&d)) return rc;
   if (d.major != 10) return fail(FQKV_ERR_DEVICE, "compute capability %d.%d is not sm_100", d.major, d.minor);
-  PipeConfig pc;
-  if (!use_pipe((int)M, (int)H, (int)N, d.sms, &pc))
-    return fail(FQKV_ERR_SCHEDULE, "no pipelined decode configuration takes M = %lld, H = %lld, N = %lld; use "
-                "fqkv_launch and fqkv_rope_split", (long long)M, (long long)H, (long long)N);
+  DecodeConfig c;
+  if (decode_pick_config((int)M, (int)H, (int)N, d.sms, &c) || c.recv_in_normed != kDecodeRecvOwn || c.grid || c.f8)
+    return fail(FQKV_ERR_SCHEDULE, "no decode configuration with the rotary epilogue takes M = %lld, H = %lld, "
+                "N = %lld; use fqkv_launch and fqkv_rope_split", (long long)M, (long long)H, (long long)N);
   const bool bf16 = dtype == FQKV_BF16;
   CUtensorMap tmW;
-  if (int rc = make_map(&tmW, weight, N, H, ldw, 128, bf16)) return rc;
-  PipeParams pp{};
-  pp.x = static_cast<const uint16_t*>(x);
-  pp.r = static_cast<const uint16_t*>(residual);
-  pp.g = rms_weight;
-  pp.gdt = rms_weight_dtype;
-  pp.rout = static_cast<uint16_t*>(residual_out);
-  pp.M = (int)M;
-  pp.H = (int)H;
-  pp.N = (int)N;
-  pp.ldx = ldx;
-  pp.ldr = ldr;
-  pp.ldo = N;
-  pp.ldro = ldro;
-  pp.eps = eps;
-  pp.kb_total = (int)((H + 63) / 64);
-  pp.nkb_max = (pp.kb_total + pc.cluster - 1) / pc.cluster;
-  pp.flags = flags;
-  pp.q = static_cast<uint16_t*>(q);
-  pp.k = static_cast<uint16_t*>(k);
-  pp.v = static_cast<uint16_t*>(v);
-  pp.cos = static_cast<const uint16_t*>(cos);
-  pp.sin = static_cast<const uint16_t*>(sin);
-  pp.S = S;
-  pp.cs_batch_stride = cos_batch == 1 ? 0 : S * head_dim;
-  pp.n_q = n_q_heads;
-  pp.n_kv = n_kv_heads;
-  pp.head_dim = head_dim;
-  const cudaError_t e = launch_pipe(pc, tmW, pp, bf16, (flags & FQKV_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+  if (int rc = make_map(&tmW, weight, N, H, ldw, 128 * decode_box_tiles(c.nt), bf16)) return rc;
+  DecodeParams dp{static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(residual), rms_weight,
+                  rms_weight_dtype, nullptr, static_cast<uint16_t*>(residual_out), (int)M, (int)H, (int)N, ldx, ldr,
+                  N, ldro, eps, (int)((H + 63) / 64), 0, flags, 0, 0, nullptr};
+  dp.nkb_max = (dp.kb_total + c.cluster - 1) / c.cluster;
+  dp.q = static_cast<uint16_t*>(q);
+  dp.k = static_cast<uint16_t*>(k);
+  dp.v = static_cast<uint16_t*>(v);
+  dp.cos = static_cast<const uint16_t*>(cos);
+  dp.sin = static_cast<const uint16_t*>(sin);
+  dp.S = S;
+  dp.cs_batch_stride = cos_batch == 1 ? 0 : S * head_dim;
+  dp.n_q = n_q_heads;
+  dp.n_kv = n_kv_heads;
+  dp.head_dim = head_dim;
+  const bool pdl = (flags & FQKV_FLAG_PDL) != 0 && (c.stages > 2 || M == 1);
+  const cudaError_t e = launch_decode(c, tmW, dp, bf16, pdl, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? 0 : cuda_fail(e, "decode kernel launch (rotary epilogue)");
 }
 
@@ -550,19 +525,6 @@ extern "C" FQKV_API int fqkv_query_schedule(int64_t M, int64_t H, int64_t N, int
     return 0;
   }
   if (sched == FQKV_SCHED_DECODE) {
-    PipeConfig pc;
-    if (use_pipe((int)M, (int)H, (int)N, d.sms, &pc)) {
-      info->block_m = pc.mpad;
-      info->block_n = 128 * pc.nt;
-      info->block_k = 64;
-      info->stages = pc.stages;
-      info->split_k = pc.cluster;
-      info->grid = (int)(((N + 128 * pc.nt - 1) / (128 * pc.nt)) * pc.cluster);
-      info->threads = kDecodeThreads;
-      info->smem_bytes = (int)pc.smem;
-      info->uses_prepass = 0;
-      return 0;
-    }
     DecodeConfig c;
     if (int rc = decode_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
     info->block_m = c.mpad;
@@ -686,31 +648,6 @@ extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const v
 
   uint16_t* normed = static_cast<uint16_t*>(workspace);
   if (sched == FQKV_SCHED_DECODE) {
-    PipeConfig pc;
-    if (use_pipe((int)M, (int)H, (int)N, d.sms, &pc)) {
-      CUtensorMap tmW;
-      if (int rc = make_map(&tmW, weight, N, H, ldw, 128, bf16)) return rc;
-      PipeParams pp{};
-      pp.x = xs;
-      pp.r = rs;
-      pp.g = rms_weight;
-      pp.gdt = rms_weight_dtype;
-      pp.out = static_cast<uint16_t*>(out);
-      pp.rout = static_cast<uint16_t*>(residual_out);
-      pp.M = (int)M;
-      pp.H = (int)H;
-      pp.N = (int)N;
-      pp.ldx = ldx;
-      pp.ldr = ldr;
-      pp.ldo = ldo;
-      pp.ldro = ldro;
-      pp.eps = eps;
-      pp.kb_total = (int)((H + 63) / 64);
-      pp.nkb_max = (pp.kb_total + pc.cluster - 1) / pc.cluster;
-      pp.flags = flags;
-      e = launch_pipe(pc, tmW, pp, bf16, pdl, st);
-      return e == cudaSuccess ? 0 : cuda_fail(e, "decode kernel launch");
-    }
     DecodeConfig c;
     if (int rc = decode_pick_config((int)M, (int)H, (int)N, d.sms, &c)) return rc;
     CUtensorMap tmW;

@@ -65,12 +65,23 @@ constexpr int kGridBatch = 8;       // grid variant: 16-byte chunks per thread l
 constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
 
 struct Layout {
-  uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, bars, tmem_slot, total;
+  uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, recvd, bars, tmem_slot, total;
 };
+
+// Receive slots of the cluster epilogue: in the ring after the partial tile (0), in the
+// normalised-activation buffer (1), or in a region of their own (2).  In the first two the
+// slots alias buffers a peer may still be using, so the cluster agrees that every CTA's MMAs
+// have retired before any copy; a region of its own takes copies at any time.
+constexpr int kRecvRing = 0, kRecvNormed = 1, kRecvOwn = kDecodeRecvOwn;
+__host__ __device__ constexpr uint32_t recv_own_bytes(int nt, int mpad) {
+  // C slots of at most 32 * ceil(nt * mpad / C) quads (shares of whole 128-row blocks)
+  return (uint32_t)(nt * mpad + kMaxCluster) * 128 * 4;
+}
 
 // f8: the ring holds e4m3 tiles (128-byte rows of two k-blocks, 128-byte swizzle); the
 // converted tiles live in TMEM.
-__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max, bool f8 = false) {
+__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max, bool f8 = false,
+                                              int recv_mode = kRecvRing) {
   Layout L;
   L.stage_bytes = nt * kWTileBytes;
   L.ring = 0;
@@ -79,7 +90,9 @@ __host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int 
   L.red = L.gain + (uint32_t)nkb_max * kKBlock * 4;    // [kMaxCluster][mpad] floats
   L.rowp = L.red + kMaxCluster * mpad * 4;            // [mpad] floats
   L.rstd = L.rowp + mpad * 4;                         // [mpad] floats
-  L.bars = (L.rstd + mpad * 4 + 7) & ~7u;   // full[S], empty[S], accum, normed, sum, part, acts, recv
+  L.recvd = (L.rstd + mpad * 4 + 15) & ~15u;          // kRecvOwn: the C receive slots
+  L.bars = (L.recvd + (recv_mode == kRecvOwn ? recv_own_bytes(nt, mpad) : 0u) + 7) & ~7u;
+  // bars: full[S], empty[S], accum, normed, sum, part, acts, recv
   L.tmem_slot = L.bars + (2 * stages + 6 + (f8 ? 2 * kConvSlots : 0)) * 8;  // + cfull, cempty
   L.total = L.tmem_slot + 16;
   return L;
@@ -137,6 +150,15 @@ __device__ __forceinline__ void convert_w8_to_tmem(const uint8_t* tile, int h, i
   tmem_st16(a_taddr + ((uint32_t)(q * 32) << 16) + 16 * hf, o);
 }
 
+// dtype(dtype(a * c) + dtype(b * s)): PyTorch's a * c + b * s on 16-bit tensors, the rounding
+// sequence of the separate rotary split (fqkv_rope.cu).
+template <typename T>
+__device__ __forceinline__ uint16_t rope_mul_add(uint16_t a, uint16_t c, uint16_t b, uint16_t s) {
+  const uint16_t x = Elem<T>::from_f(__fmul_rn(Elem<T>::to_f(a), Elem<T>::to_f(c)));
+  const uint16_t y = Elem<T>::from_f(__fmul_rn(Elem<T>::to_f(b), Elem<T>::to_f(s)));
+  return Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(x), Elem<T>::to_f(y)));
+}
+
 __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
 }
@@ -147,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   FQKV_TRACE_DECL
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = make_layout(stages, NT, MPAD, p.nkb_max, F8);
+  const Layout L = make_layout(stages, NT, MPAD, p.nkb_max, F8, p.recv_in_normed);
   uint8_t* ring = smem + L.ring;
   uint8_t* normed = smem + L.normed;
   float* red = reinterpret_cast<float*>(smem + L.red);
@@ -171,7 +193,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // when they fit there (else after the partial tile in the ring).
   float* part = reinterpret_cast<float*>(ring);
   constexpr uint32_t kPartBytes = NT * MPAD * kTileRows * 4;
-  uint8_t* recv = p.recv_in_normed ? normed : ring + kPartBytes;
+  uint8_t* recv = p.recv_in_normed == kRecvNormed ? normed
+                 : p.recv_in_normed == kRecvOwn  ? smem + L.recvd
+                                                 : ring + kPartBytes;
+  const bool recv_own = p.recv_in_normed == kRecvOwn;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // C CTAs split K: the CTAs of a cluster, or (GRID) blockIdx.x of a row of independent CTAs.
@@ -179,6 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = GRID ? blockIdx.x : cluster_ctarank();
   static_assert(!(GRID && (F8 || MPAD != 16)), "the grid variant takes 16-bit weights and at most 16 rows");
   static_assert(kNormWarps <= kMaxCluster, "the grid variant's per-warp row sums use the cluster sum slots");
+  // Hand-offs wait by polling their mbarrier (test_wait) when p.poll, else in try_wait.
   const int KB = p.kb_total;
   const int kb0 = (int)((rank * (uint32_t)KB) / C), kb1 = (int)(((rank + 1) * (uint32_t)KB) / C);
   const int nkb = kb1 - kb0;
@@ -209,6 +235,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(recv_bar, 1);     // local arrive + the peers' bulk copies (complete_tx)
     fence_mbarrier_init_cluster();
   }
+  const int nstage = F8 ? (nkb + 1) / 2 : nkb;  // e4m3: a ring stage holds two k-blocks
+  auto issue_stage = [&](int i, int s, uint64_t pol_w) {
+    mbar_arrive_expect_tx(&full[s], L.stage_bytes);
+    // A stage holds NT 128-row tiles: one box of NT x 128 rows for NT <= 2, else NT boxes
+    // of 128 rows (a TMA box dimension is at most 256).
+#pragma unroll
+    for (int j = 0; j < NT; j += kBoxTiles)
+      tma_load_2d_hint(ring + s * L.stage_bytes + j * kWTileBytes, &tmW, &full[s], (kb0 + (F8 ? 2 * i : i)) * kKBlock,
+                       n_base + j * kTileRows, pol_w);
+  };
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tmW);
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -224,30 +260,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint32_t tx = L.stage_bytes;
       // The weight does not depend on the preceding grid when the caller says so: start
       // streaming it before that grid has finished.  Only `pre` stages go out before the
       // norm warps have requested their activations, so those small, latency-critical
       // loads are not queued behind megabytes of weight in the memory system.
       if (!(p.flags & FQKV_FLAG_STATIC_WEIGHTS)) pdl_wait();
-      const int pre = min(F8 ? (nkb + 1) / 2 : nkb, min(stages, p.pre_stages));
+      const int pre = min(nstage, min(stages, p.pre_stages));
       const uint64_t pol_w = policy_evict_first();
       bool ok = true;
       int s = 0, round = 0, issued = 0;
-      const int nstage = F8 ? (nkb + 1) / 2 : nkb;  // e4m3: a ring stage holds two k-blocks
       for (int i = 0; i < nstage; ++i) {
         if (i == pre) {
           ok = mbar_wait(acts_bar, 0);
           FQKV_TRACE_POINT(5);
         }
         if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
-        mbar_arrive_expect_tx(&full[s], tx);
-        // A stage holds NT 128-row tiles: one box of NT x 128 rows for NT <= 2, else NT
-        // boxes of 128 rows (a TMA box dimension is at most 256).
-#pragma unroll
-        for (int j = 0; j < NT; j += kBoxTiles)
-          tma_load_2d_hint(ring + s * L.stage_bytes + j * kWTileBytes, &tmW, &full[s],
-                           (kb0 + (F8 ? 2 * i : i)) * kKBlock, n_base + j * kTileRows, pol_w);
+        issue_stage(i, s, pol_w);
         if (i == 0) FQKV_TRACE_POINT(4);
         ++issued;
         if (++s == stages) {
@@ -334,9 +362,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // The tile's partial sums are reduced in 16-byte quads (4 output features): quad
     // f = ((m * NT + nt) * 128 + row) / 4 for token m < M; rank o reduces [F(o), F(o+1)).
+    // With the rotary split, shares are whole 128-row blocks (m, nt): a head's two halves stay
+    // with one CTA.
+    const bool rope = p.q != nullptr;
     const uint32_t total4 = (uint32_t)(NT * p.M * (kTileRows / 4));
-    auto share = [&](uint32_t o) { return (o * total4) / C; };
-    const uint32_t slot_bytes = 16u * ((NT * MPAD * (kTileRows / 4) + C - 1) / C);
+    auto share = [&](uint32_t o) {
+      return rope ? (o * (uint32_t)(NT * p.M)) / C * (kTileRows / 4) : (o * total4) / C;
+    };
+    const uint32_t slot_bytes = rope ? 16u * (kTileRows / 4) * ((NT * MPAD + C - 1) / C)
+                                     : 16u * ((NT * MPAD * (kTileRows / 4) + C - 1) / C);
     // This CTA expects C * MPAD row sums (4 bytes each) from the cluster's st.async writes,
     // and later C - 1 bulk copies of its share of the tile.
     if (!GRID && et == 0) {
@@ -714,11 +748,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // thread 0's cluster fence, which the relaxed remote arrives then publish.  An arrival
       // also says that this CTA's MMAs have retired, so its ring may receive the peers' slices.
       asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (et == 0) {
-        fence_acq_rel_cluster();
-        for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
+      if (!recv_own) {
+        if (et == 0) {
+          fence_acq_rel_cluster();
+          for (uint32_t c = 0; c < C; ++c) mbar_arrive_remote_relaxed(mapa_shared(smem_u32(part_bar), c));
+        }
+        ok = mbar_wait<true>(part_bar, 0) && ok;
       }
-      ok = mbar_wait<true>(part_bar, 0) && ok;
       if (et == 0) FQKV_TRACE_POINT(14);
       // Lane c of warp 2 sends rank c's share of this CTA's partial tile to slot `rank` of
       // rank c's ring.
@@ -731,12 +767,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait<true>(recv_bar, 0) && ok;
       if (et == 0) FQKV_TRACE_POINT(15);
       // Every copy into this CTA has landed, so their sources have been read: this thread
-      // makes no further access to a peer's shared memory, nor a peer to this CTA's.
-      cluster_arrive_release_thread();
+      // makes no further access to a peer's shared memory, nor a peer to this CTA's.  The
+      // barrier only has to order execution (the copies' data is tracked by their mbarriers).
+      cluster_arrive_relaxed_thread();
       // Reduce this CTA's share: the C partials of each quad in rank order (deterministic).
       const uint32_t f0 = share(rank), f1 = share(rank + 1);
       const float4* part4 = reinterpret_cast<const float4*>(part);
       const float4* recv4 = reinterpret_cast<const float4*>(recv);
+      // Rotary split: the rounded outputs of this CTA's blocks go to its own (unused) receive
+      // slot, [local block][128] in the dtype, then out head-major.
+      uint16_t* tout = reinterpret_cast<uint16_t*>(recv + rank * slot_bytes);
       for (uint32_t f = f0 + et; f < f1; f += kNormThreads) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (uint32_t c = 0; c < C; ++c) {
@@ -746,7 +786,52 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc.z += v.z;
           acc.w += v.w;
         }
-        store_quad(f, acc);
+        if (rope)
+          *reinterpret_cast<uint2*>(tout + (f - f0) * 4) =
+              make_uint2(Elem<T>::from_f2(acc.x, acc.y), Elem<T>::from_f2(acc.z, acc.w));
+        else
+          store_quad(f, acc);
+      }
+      if (rope) {
+        // Head-major Q / K / V with the rotary embedding on Q and K, 8 features per thread
+        // (the rounding sequence of fqkv_rope.cu: each product rounded to the dtype, their
+        // fp32 sum rounded).
+        __syncwarp();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        const int d = p.head_dim, hd = d / 2;
+        const uint32_t b0 = f0 / (kTileRows / 4), nblk = (f1 - f0) / (kTileRows / 4);
+        for (uint32_t u = et; u < nblk * (kTileRows / 8); u += kNormThreads) {
+          const uint32_t lb = u / (kTileRows / 8);
+          const int r8 = (int)(u - lb * (kTileRows / 8)) * 8;
+          const uint32_t mn = b0 + lb;
+          const int nt = (int)(mn % NT), m = (int)(mn / NT);
+          const int nn = n_base + nt * kTileRows + r8;
+          if (nn >= p.N) continue;
+          const int head = nn / d, j = nn - head * d;  // the 8 features stay in one half of a head
+          const int64_t b = m / p.S, sq = m - b * p.S;
+          const uint16_t* blk = tout + lb * kTileRows;
+          uint16_t xv[8], ov[8];
+          *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(blk + r8);
+          uint16_t* dst;
+          if (head < p.n_q + p.n_kv) {
+            uint16_t yv[8], cv[8], sv[8];
+            *reinterpret_cast<uint4*>(yv) = *reinterpret_cast<const uint4*>(blk + (r8 ^ hd));  // other half
+            const int64_t cs = b * p.cs_batch_stride + sq * d + j;
+            *reinterpret_cast<uint4*>(cv) = __ldg(reinterpret_cast<const uint4*>(p.cos + cs));
+            *reinterpret_cast<uint4*>(sv) = __ldg(reinterpret_cast<const uint4*>(p.sin + cs));
+            const bool first = j < hd;
+#pragma unroll
+            for (int e = 0; e < 8; ++e)  // first half: x * cos + (-y) * sin; second: x * cos + y * sin
+              ov[e] = rope_mul_add<T>(xv[e], cv[e], first ? (uint16_t)(yv[e] ^ 0x8000u) : yv[e], sv[e]);
+            dst = head < p.n_q ? p.q + ((b * p.n_q + head) * p.S + sq) * d
+                               : p.k + ((b * p.n_kv + (head - p.n_q)) * p.S + sq) * d;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ov[e] = xv[e];
+            dst = p.v + ((b * p.n_kv + (head - p.n_q - p.n_kv)) * p.S + sq) * d;
+          }
+          *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(ov);
+        }
       }
       if (et == 0) FQKV_TRACE_POINT(16);
     }
@@ -757,7 +842,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < 2) {
     __syncwarp();
     tc_fence_before();
-    cluster_arrive_release_thread();
+    cluster_arrive_relaxed_thread();
   }
   // No CTA leaves while a peer may still read its shared memory.
   cluster_wait_acquire_thread();
@@ -862,7 +947,7 @@ constexpr size_t kSmemLimit = 232448;  // max dynamic shared memory per block on
 
 size_t decode_smem_bytes(const DecodeConfig& c, int kb_total) {
   const int nkb_max = (kb_total + c.cluster - 1) / c.cluster;
-  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8 != 0).total;
+  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8 != 0, c.recv_in_normed).total;
 }
 
 // Choose (tile rows, cluster size, ring depth).  Candidates must fit shared memory and
@@ -876,13 +961,20 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, boo
   static const int force_nt = env_int("FQKV_DECODE_NT", 0);
   static const int force_c = env_int("FQKV_DECODE_CLUSTER", 0);
   static const int force_s = env_int("FQKV_DECODE_STAGES", 0);
+  // The epilogue's receive slots: a region of their own for 16-bit weights and up to 32 rows
+  // (measured on B200, Llama-3-8B, graph-timed: M = 16 13.28 -> 12.72 us, M = 1 12.40 ->
+  // 12.15 us against slots aliasing the ring / the activations, which need the cluster to
+  // agree first that every CTA's MMAs have retired); FQKV_DECODE_RECV=1 forces the aliasing
+  // slots (comparisons).
+  static const int recv_mode_env = env_int("FQKV_DECODE_RECV", 0);
   // The search below queries occupancy for many candidates; its result is cached per
   // (device, MPAD, H, N, SM count, overrides), so a model's per-step calls skip it.
   static std::mutex mu;
   static std::map<std::tuple<int, int, int, int, int, int, int, int, int>, std::pair<int, DecodeConfig>> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, mpad, H, N, sm_count, force_nt, force_c, force_s, f8 ? 1 : 0);
+  const auto key = std::make_tuple(dev, mpad, H, N, sm_count, force_nt, force_c, force_s * 4 + recv_mode_env,
+                                   f8 ? 1 : 0);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -902,26 +994,37 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, boo
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
       if ((KB + cl - 1) / cl * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
-      // The epilogue's partial tile aliases the ring; its C receive slots go into the
-      // normalised-activation buffer when they fit there, else after the partial tile.
+      // The epilogue's partial tile aliases the ring.  Its C receive slots get a region of
+      // their own (16-bit weights, up to 32 rows) when that still leaves a ring of three
+      // stages or more; otherwise they go into the normalised-activation buffer when they fit
+      // there, else after the partial tile in the ring.
       const int part_bytes = nt * mpad * kTileRows * 4;
       const int recv_bytes = cl * 16 * ((nt * mpad * (kTileRows / 4) + cl - 1) / cl);
-      const int recv_in_normed = recv_bytes <= (KB + cl - 1) / cl * mpad * 128 ? 1 : 0;
-      const int epi_bytes = part_bytes + (recv_in_normed ? 0 : recv_bytes);
-      const int min_stages = (epi_bytes + nt * tile_bytes - 1) / (nt * tile_bytes);
-      for (int st = 16; st >= max(2, min_stages); --st) {
-        if (force_s && st != force_s) continue;
-        DecodeConfig t{mpad, nt, st, cl, 0, recv_in_normed, f8 ? 1 : 0};
-        t.smem = decode_smem_bytes(t, KB);
-        if (t.smem > kSmemLimit) continue;
-        const int resident = max_active_clusters(t, tiles);
-        if (resident < tiles) continue;  // would need a second wave
-        const long score = (long)tiles * cl * 64 + st;
-        if (score > best_score) {
-          best_score = score;
-          best = t;
+      const int alias_mode = recv_bytes <= (KB + cl - 1) / cl * mpad * 128 ? kRecvNormed : kRecvRing;
+      // Deepest resident ring of a receive mode for this (nt, cl), or a config with stages 0.
+      auto deepest = [&](int mode) {
+        const int epi_bytes = part_bytes + (mode == kRecvRing ? recv_bytes : 0);
+        const int min_stages = (epi_bytes + nt * tile_bytes - 1) / (nt * tile_bytes);
+        for (int st = 16; st >= max(2, min_stages); --st) {
+          if (force_s && st != force_s) continue;
+          DecodeConfig t{mpad, nt, st, cl, 0, mode, f8 ? 1 : 0};
+          t.smem = decode_smem_bytes(t, KB);
+          if (t.smem > kSmemLimit) continue;
+          if (max_active_clusters(t, tiles) < tiles) continue;  // would need a second wave
+          return t;
         }
-        break;  // deepest ring that fits for this (nt, cl)
+        return DecodeConfig{mpad, nt, 0, cl, 0, mode, f8 ? 1 : 0};
+      };
+      DecodeConfig t = deepest(alias_mode);
+      if (recv_mode_env != 1 && !f8 && mpad <= 32) {
+        const DecodeConfig own = deepest(kRecvOwn);
+        if (own.stages >= 3 || (own.stages > 0 && t.stages == 0)) t = own;
+      }
+      if (t.stages == 0) continue;
+      const long score = (long)tiles * cl * 64 + t.stages;
+      if (score > best_score) {
+        best_score = score;
+        best = t;
       }
     }
   }

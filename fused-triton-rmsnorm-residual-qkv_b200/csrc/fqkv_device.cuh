@@ -69,14 +69,17 @@ __device__ __forceinline__ unsigned long long clock64_now() {
       }                                                                                                  \
     }                                                                                                    \
   } while (0)
+// Only after the barrier that follows FQKV_TRACE_BEGIN (the record index is in shared memory);
+// the index is checked against the buffer's capacity before any write.
 #define FQKV_TRACE_POINT(slot)                                                                           \
   do {                                                                                                   \
-    if (fqkv_trace_idx_ != 0xFFFFFFFFu)                                                                  \
-      ::fqkv::g_trace_buf[(size_t)fqkv_trace_idx_ * ::fqkv::kTraceSlots + (slot)] = ::fqkv::clock64_now(); \
+    const unsigned int fqkv_ti_ = fqkv_trace_idx_;                                                       \
+    if (fqkv_ti_ < ::fqkv::g_trace_cap && ::fqkv::g_trace_buf)                                           \
+      ::fqkv::g_trace_buf[(size_t)fqkv_ti_ * ::fqkv::kTraceSlots + (slot)] = ::fqkv::clock64_now();      \
   } while (0)
 #define FQKV_TRACE_END()                                                                                 \
   do {                                                                                                   \
-    if (fqkv_trace_idx_ != 0xFFFFFFFFu) {                                                                \
+    if (fqkv_trace_idx_ < ::fqkv::g_trace_cap && ::fqkv::g_trace_buf) {                                  \
       unsigned long long g1;                                                                             \
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));                                             \
       unsigned long long* r = ::fqkv::g_trace_buf + (size_t)fqkv_trace_idx_ * ::fqkv::kTraceSlots;       \
@@ -327,6 +330,10 @@ __device__ __forceinline__ void cluster_sync() {
 // reach them at different points.
 __device__ __forceinline__ void cluster_arrive_release_thread() {
   asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+// Arrival that orders nothing: for barriers that only have to synchronise execution.
+__device__ __forceinline__ void cluster_arrive_relaxed_thread() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire_thread() {
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");

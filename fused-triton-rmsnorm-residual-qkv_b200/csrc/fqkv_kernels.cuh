@@ -71,27 +71,9 @@ struct DecodeParams {
   // arrival counter per tile group (zero on entry, left zero on exit).
   float* gpart;
   int* gcnt;
-};
-
-// Pipelined decode kernel (fqkv_decode_pipe.cu): 16-bit weights, M <= 32.
-struct PipeParams {
-  const uint16_t* x;
-  const uint16_t* r;  // nullable
-  const void* g;
-  int gdt;
-  uint16_t* out;      // [M, N] row stride ldo (unused when q is set)
-  uint16_t* rout;     // nullable
-  int M, H, N;
-  int64_t ldx, ldr, ldo, ldro;
-  float eps;
-  int kb_total;       // ceil(H / 64)
-  int nkb_max;        // max k-blocks of one CTA's K slice
-  int flags;
-  int pre_stages;     // weight stages issued before the activation loads are in, once the
-                      // preceding grid has completed
-  // Rotary split (optional): with q set, the output is written head-major as q [B, n_q, S, d],
-  // k and v [B, n_kv, S, d] (token m = b * S + s), with the rotary embedding on q and k
-  // (cos / sin [B or 1, S, d]), instead of `out`.
+  // Rotary split (cluster kernel, 16-bit weights, own receive slots): with q set, the output
+  // is written head-major as q [B, n_q, S, d], k and v [B, n_kv, S, d] (token m = b * S + s),
+  // with the rotary embedding on q and k (cos / sin [B or 1, S, d]), instead of `out`.
   uint16_t* q;
   uint16_t* k;
   uint16_t* v;
@@ -362,6 +344,10 @@ struct DecodeConfig {
 };
 
 int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, bool f8 = false);
+// DecodeConfig::recv_in_normed value of the receive slots in a region of their own (the
+// epilogue needs no cluster agreement before its copies; the rotary split needs these).
+constexpr int kDecodeRecvOwn = 2;
+constexpr int kDecodeRopeMaxM = 32;  // the rotary-split epilogue: 16-bit weights, own slots
 // Grid variant of the fused decode kernel: every CTA reads whole activation rows, so it
 // serves few rows only.
 constexpr int kGridMaxM = 8;
@@ -377,19 +363,6 @@ __host__ __device__ constexpr int decode_box_tiles(int nt) { return nt <= 2 ? nt
 size_t decode_smem_bytes(const DecodeConfig& c, int kb_total);
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream);
-
-struct PipeConfig {
-  int mpad;     // token columns of the MMA (16 or 32)
-  int nt;       // 128-row weight tiles per CTA (1 to 5), accumulated one after the other
-  int stages;   // ring depth (16 KB stages)
-  int cluster;  // CTAs splitting K (cluster size)
-  size_t smem;  // dynamic shared memory bytes
-};
-constexpr int kPipeMaxM = 32;
-int pipe_pick_config(int M, int H, int N, int sm_count, PipeConfig* cfg);
-size_t pipe_smem_bytes(const PipeConfig& c, int kb_total);
-cudaError_t launch_pipe(const PipeConfig& c, const CUtensorMap& tmW, const PipeParams& p, bool bf16, bool pdl,
-                        cudaStream_t stream);
 
 constexpr int kStreamKMaxGrid = 320;  // partial-slot capacity of the workspace (>= 2 x SM count)
 struct StreamKConfig {

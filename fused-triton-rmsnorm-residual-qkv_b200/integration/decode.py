@@ -47,6 +47,24 @@ class GraphedGreedyDecoder:
         self._pos.add_(1)
 
     @torch.no_grad()
+    def forced_logits(self, prompt: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
+        """Teacher forcing, eagerly: the fp32 logits that predict ``tokens[:, t]`` for every t
+        ((batch, n, vocab)), when ``tokens[:, :t]`` follow ``prompt``.  Comparing two models on
+        the same token sequence separates numerical differences from the divergence of their
+        own greedy paths."""
+        B, P = prompt.shape
+        n = tokens.shape[1]
+        cache = self._new_cache()
+        pos = torch.arange(P, device=self.device)[None].expand(B, P)
+        out = self.model(input_ids=prompt, position_ids=pos, past_key_values=cache, use_cache=True)
+        logits = [out.logits[:, -1, :].float()]
+        for t in range(n - 1):
+            p = torch.full((B, 1), P + t, dtype=torch.long, device=self.device)
+            out = self.model(input_ids=tokens[:, t:t + 1], position_ids=p, past_key_values=cache, use_cache=True)
+            logits.append(out.logits[:, -1, :].float())
+        return torch.stack(logits, dim=1)
+
+    @torch.no_grad()
     def generate(self, prompt: torch.Tensor, n_new: int) -> torch.Tensor:
         B, P = prompt.shape
         if B != self.batch or P + n_new > self.max_len:

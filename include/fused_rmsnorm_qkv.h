@@ -153,7 +153,7 @@ FQKV_API int fqkv_query_schedule(int64_t M, int64_t H, int64_t N, int dtype, int
  *                with M = B * S tokens (row m = b * S + s) and N = (n_q + 2 n_kv) * head_dim
  *   q     [B, n_q, S, head_dim]   k, v  [B, n_kv, S, head_dim]   dtype, contiguous
  *   cos, sin  [cos_batch, S, head_dim] dtype, contiguous; cos_batch is 1 (shared) or B
- * Decode sizes only: M <= 32, head_dim 64 or 128, and a configuration of the pipelined
+ * Decode sizes only: M <= 32, head_dim 64 or 128, and a configuration of the fused
  * decode kernel that fits the device; otherwise FQKV_ERR_SCHEDULE (run fqkv_launch and
  * fqkv_rope_split).  All tensors 16-byte aligned.  Needs no workspace.
  */

@@ -1,9 +1,19 @@
 """End-to-end check of the integration in a KV-cache decode loop: greedy decoding with a
 static KV cache, one token per step replayed from a CUDA graph
-(``integration.GraphedGreedyDecoder``), on a Llama-3-8B-shaped model with random weights.
-The patched model (the reference's Q/K/V patch, and the fullest mode: cross-layer fusion
-with the one-launch rotary split) must produce the unpatched model's greedy tokens for
-every step."""
+(``integration.GraphedGreedyDecoder``), on a Llama-3-8B-shaped model with random weights,
+for the reference's Q/K/V patch and the fullest mode (cross-layer fusion with the rotary
+split in the projection's epilogue).
+
+The fused op normalises as the reference's kernel does -- dtype((h * rstd) * g), one
+rounding -- while the model's own RMSNorm rounds h * rstd to the dtype before the gain, so
+patched and unpatched logits differ by rounding noise, and with random weights a greedy
+path can flip where two logits are within that noise.  So, on the unpatched model's
+greedy tokens (teacher forcing), the patched logits must stay within a small fraction of
+the logit spread, and every step where the argmax differs must be a near tie that this
+noise explains; the patched greedy tokens must equal the unpatched ones up to the first
+such near tie.  Separately, the graph-replayed loop must reproduce the same model's eager
+greedy decode exactly.
+"""
 from __future__ import annotations
 
 import pytest
@@ -14,17 +24,46 @@ from integration import GraphedGreedyDecoder, build_llama3_8b, fused_patch
 pytestmark = pytest.mark.gpu
 
 
+def _eager_greedy(dec, prompt, n_new):
+    """Greedy tokens from teacher forcing on the model's own choices (no graph)."""
+    tokens = torch.empty(prompt.shape[0], 0, dtype=torch.long, device=prompt.device)
+    for _ in range(n_new):
+        logits = dec.forced_logits(prompt, torch.cat([tokens, tokens[:, :1]], dim=1))  # last column unused
+        tokens = torch.cat([tokens, logits[:, tokens.shape[1]].argmax(-1, keepdim=True)], dim=1)
+    return tokens
+
+
 @pytest.mark.parametrize("batch", [1, 4])
-def test_patched_greedy_decode_matches_unpatched(batch):
+def test_patched_decode_loop_tracks_the_unpatched_model(batch):
     model = build_llama3_8b(dtype=torch.bfloat16, device="cuda", num_hidden_layers=2)
     gen = torch.Generator(device="cuda").manual_seed(3 + batch)
     prompt = torch.randint(0, model.config.vocab_size, (batch, 12), generator=gen, device="cuda")
     n_new = 20
-    ref = GraphedGreedyDecoder(model, batch, 64).generate(prompt, n_new)
+    dec = GraphedGreedyDecoder(model, batch, 64)
+    ref = dec.generate(prompt, n_new)
     assert ref.shape == (batch, n_new)
+    ref_logits = dec.forced_logits(prompt, ref)
+    assert torch.equal(ref_logits.argmax(-1), ref)  # the graph loop decodes what eager forcing predicts
+    spread = (ref_logits.amax(-1) - ref_logits.amin(-1)).mean()
     for kw in ({}, {"cross_layer": True, "rope": True}):
         with fused_patch(model, **kw):
-            got = GraphedGreedyDecoder(model, batch, 64).generate(prompt, n_new)
-        assert torch.equal(got, ref), (kw, got, ref)
+            got = dec.generate(prompt, n_new)
+            logits = dec.forced_logits(prompt, ref)
+            if batch == 1:
+                assert torch.equal(got, _eager_greedy(dec, prompt, n_new)), kw  # loop == eager, same model
+        diff = (logits - ref_logits).abs()
+        assert float(diff.max()) < 0.05 * float(spread), (kw, float(diff.max()), float(spread))
+        top2 = ref_logits.topk(2, dim=-1)
+        margin = top2.values[..., 0] - top2.values[..., 1]
+        noise = 2 * diff.amax(-1)
+        flips = logits.argmax(-1) != ref
+        assert bool((margin[flips] <= noise[flips]).all()), (kw, margin[flips], noise[flips])
+        for b in range(batch):
+            same = (got[b] == ref[b]).long().cumprod(0)
+            first = int(same.sum())
+            if first < n_new:  # the greedy paths part only at a near tie of the unpatched logits
+                assert float(margin[b, first]) <= float(noise[b, first]), (kw, b, first)
+        print(kw, "max logit diff", float(diff.max()), "spread", float(spread),
+              "equal greedy steps", [int((got[b] == ref[b]).long().cumprod(0).sum()) for b in range(batch)])
     del model
     torch.cuda.empty_cache()
