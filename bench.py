@@ -503,6 +503,7 @@ def run_detail(wl_default: dict, dev, peaks: dict, args_triton_comparator: str =
         detail[label] = entry
         del ss
     detail.update(run_fp8w_detail(dev, peaks))
+    detail["llama3-8b_decode_rope"] = run_rope_detail(dev)
     if args_triton_comparator != "off":
         detail["reference_triton"] = run_reference_triton_detail(dev, peaks, args_triton_comparator == "autotune")
     detail["llama3-8b_layer_stack"] = run_layer_stack(dev)
@@ -534,6 +535,49 @@ def run_fp8w_detail(dev, peaks: dict) -> dict:
             "M": mm, "H": H, "N": N, "dtype": "bf16 activations, e4m3 weight", "us": round(t_ms * 1e3, 3),
             "GB/s": round(b / t_ms / 1e6, 1), "pct_of_measured_hbm": round(100 * b / t_ms / 1e6 / peaks["hbm_gbs"], 2)}
         del q8
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_rope_detail(dev, ms=(1, 16)) -> dict:
+    """The Q/K/V split + rotary embedding (llama3_patch.py:148-168) on the Llama-3-8B decode
+    shape, M sequences of one token each at their own positions, graph-timed like the rows
+    above: the projection alone, the projection followed by the separate rotary split
+    (two launches), and the rotary split in the projection's epilogue (one launch)."""
+    from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul, fused_add_rmsnorm_qkv_rope, qkv_rope_split
+
+    wl = dict(WORKLOADS["llama3-8b-decode"], sets=32)
+    out = {"unit": "us per step", "shape": "M sequences x 1 token, H 4096, 32 q / 8 kv heads of 128, bf16"}
+    for mm in ms:
+        ss, layout = make_sets(wl, mm, torch.bfloat16, dev, 1, 0, wl["sets"])
+        gen = torch.Generator(device=dev).manual_seed(5)
+        pos = torch.randint(0, 4096, (mm,), generator=gen, device=dev).float()
+        inv = 1.0 / (500000.0 ** (torch.arange(0, wl["d"], 2, device=dev).float() / wl["d"]))
+        ang = torch.cat([pos[:, None] * inv[None]] * 2, dim=-1)[:, None, :]  # (M, 1, d)
+        cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+        sets = [(x.view(mm, 1, -1), r.view(mm, 1, -1), g, w) for (x, r, g, w) in ss]
+        del ss
+        nq, nkv, eps = wl["n_q"], wl["n_kv"], wl["eps"]
+
+        def alone(i):
+            x, r, g, w = sets[i % len(sets)]
+            fused_add_rmsnorm_matmul(x, r, g, w, eps, static_weights=True)
+
+        def two(i):
+            x, r, g, w = sets[i % len(sets)]
+            qkv, _ = fused_add_rmsnorm_matmul(x, r, g, w, eps, static_weights=True)
+            qkv_rope_split(qkv, cos, sin, nq, nkv)
+
+        def one(i):
+            x, r, g, w = sets[i % len(sets)]
+            fused_add_rmsnorm_qkv_rope(x, r, g, w, cos, sin, nq, nkv, eps=eps, static_weights=True)
+
+        row = {}
+        for name, fn in (("projection_only", alone), ("projection_then_rope_split", two), ("fused_rope", one)):
+            row[name] = round(time_graph(fn, 1000, 5, dev, replays=10) / 1000 * 1e3, 3)
+        row["fused_rope_over_projection_only"] = round(row["fused_rope"] - row["projection_only"], 3)
+        out[f"M{mm}"] = row
+        del sets
         torch.cuda.empty_cache()
     return out
 
@@ -584,7 +628,12 @@ def run_kv_decode(dev, n_layers: int = 4, batches=(1, 16), prompt_len: int = 128
     e2e_decode.py (prompt 128, 256 new tokens, batch 1 and 16, tokens per second over the
     decode phase) with each decode step replayed from a CUDA graph
     (integration.GraphedGreedyDecoder).  Unpatched against the patch's modes; each patched
-    run's tokens are compared with the unpatched run's."""
+    run's tokens are compared with the unpatched run's.  A random-init model's next-token
+    distribution is nearly flat, so a last-bit difference in one step can flip a greedy
+    choice and the two free-running sequences part for good; each mode is therefore also
+    run teacher-forced on the unpatched tokens, and the rows report how often its greedy
+    choice agrees with the unpatched one given the same prefix, and the largest logit
+    difference."""
     from contextlib import nullcontext
 
     from integration import GraphedGreedyDecoder, build_llama3_8b, fused_patch
@@ -597,7 +646,7 @@ def run_kv_decode(dev, n_layers: int = 4, batches=(1, 16), prompt_len: int = 128
         for B in batches:
             gen = torch.Generator(device=dev).manual_seed(11)
             prompt = torch.randint(0, model.config.vocab_size, (B, prompt_len), generator=gen, device=dev)
-            row, ref_tokens = {}, None
+            row, ref_tokens, ref_forced = {}, None, None
             for name, kw in modes:
                 with (nullcontext() if kw is None else fused_patch(model, **kw)):
                     dec = GraphedGreedyDecoder(model, B, prompt_len + n_new)
@@ -605,17 +654,26 @@ def run_kv_decode(dev, n_layers: int = 4, batches=(1, 16), prompt_len: int = 128
                     for _ in range(repeats):
                         tokens = dec.generate(prompt, n_new)
                         secs.append(dec.decode_seconds)
+                    forced = dec.forced_logits(prompt, tokens if ref_tokens is None else ref_tokens)
                 steps = n_new - 2
                 t = statistics.median(secs)
                 entry = {"tok_per_s": round(B * steps / t, 1), "us_per_step": round(t / steps * 1e6, 2)}
                 if ref_tokens is None:
-                    ref_tokens = tokens
+                    ref_tokens, ref_forced = tokens, forced
+                    entry["teacher_forced_argmax_equals_own_tokens"] = round(
+                        float((forced.argmax(-1) == tokens).float().mean()), 4)
                 else:
                     same = (tokens == ref_tokens).all(dim=0)
                     entry["tokens_equal_unpatched"] = bool(same.all())
                     entry["steps_equal_before_first_difference"] = int(same.long().cumprod(0).sum())
+                    entry["teacher_forced_argmax_agreement"] = round(
+                        float((forced.argmax(-1) == ref_tokens).float().mean()), 4)
+                    entry["teacher_forced_max_abs_logit_diff"] = round(float((forced - ref_forced).abs().max()), 4)
+                    entry["logit_std"] = round(float(ref_forced.std()), 4)
+                del forced
                 row[name] = entry
             out[f"batch{B}"] = row
+            del ref_forced
     del model
     torch.cuda.empty_cache()
     return out

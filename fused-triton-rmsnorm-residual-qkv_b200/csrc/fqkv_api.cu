@@ -318,9 +318,10 @@ extern "C" FQKV_API int fqkv_trace_attach(void* buf, unsigned int records) {
 // embedding on Q and K (fqkv_rope.cu): what llama3_patch.py:156-168 does in PyTorch after
 // the fused call (split, view as heads, transpose, apply_rotary_pos_emb).
 // The op with e4m3 weights and an fp32 scale per weight row: the fused decode kernel
-// streams the one-byte weight and converts it exactly to the dtype in shared memory, and
-// the row scale multiplies the k-summed value once.  Decode schedule only (M <= 64 with a
-// fitting configuration).
+// streams the one-byte weight into e4m3 x e4m3 tensor-core MMAs against the normalised
+// activations split exactly into e4m3 terms (a power-of-two scale per token), and the row
+// scale multiplies the k-summed value once.  Decode schedule only (M <= 64 with a fitting
+// configuration).
 extern "C" FQKV_API int fqkv_launch_fp8w(const void* x, const void* residual, const void* rms_weight,
                                          int rms_weight_dtype, const void* weight, const float* weight_scale,
                                          void* out, void* residual_out, int64_t M, int64_t H, int64_t N, int64_t ldx,
@@ -347,10 +348,26 @@ extern "C" FQKV_API int fqkv_launch_fp8w(const void* x, const void* residual, co
   if (int rc = device_info(&d)) return rc;
   if (d.major != 10) return fail(FQKV_ERR_DEVICE, "compute capability %d.%d is not sm_100", d.major, d.minor);
   DecodeConfig c;
-  if (decode_pick_config((int)M, (int)H, (int)N, d.sms, &c, true))
+  if (decode_pick_config((int)M, (int)H, (int)N, d.sms, &c, decode_f8_terms(dtype == FQKV_BF16))) {
+    // More than 32 rows: the activations' e4m3 terms of a K slice may not fit beside the
+    // ring (fp16 takes three terms per value).  The rows are independent, so the first 32
+    // and the rest run as two launches (each streams the weight once).
+    if (M > 32 && decode_pick_config(32, (int)H, (int)N, d.sms, &c, decode_f8_terms(dtype == FQKV_BF16)) == 0) {
+      const char* xb = static_cast<const char*>(x);
+      const char* rb = static_cast<const char*>(residual);
+      char* ob2 = static_cast<char*>(out);
+      char* rob2 = static_cast<char*>(residual_out);
+      if (int rc = fqkv_launch_fp8w(x, residual, rms_weight, rms_weight_dtype, weight, weight_scale, out,
+                                    residual_out, 32, H, N, ldx, ldr, ldw, ldo, ldro, eps, dtype, flags, stream))
+        return rc;
+      return fqkv_launch_fp8w(xb + 32 * ldx * 2, rb ? rb + 32 * ldr * 2 : nullptr, rms_weight, rms_weight_dtype, weight,
+                              weight_scale, ob2 + 32 * ldo * 2, rob2 ? rob2 + 32 * ldro * 2 : nullptr, M - 32, H, N,
+                              ldx, ldr, ldw, ldo, ldro, eps, dtype, flags, stream);
+    }
     return fail(FQKV_ERR_SCHEDULE,
                 "no fused decode configuration takes M = %lld, H = %lld, N = %lld with e4m3 weights (M <= 64)",
                 (long long)M, (long long)H, (long long)N);
+  }
   CUtensorMap tmW;
   if (int rc = make_map(&tmW, weight, N, H, ldw, 128 * decode_box_tiles(c.nt), kMapE4M3)) return rc;
   DecodeParams dp{static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(residual), rms_weight,

@@ -23,10 +23,12 @@
 //              the slice of its partial tile that rank o owns into rank o's idle buffers
 //              (cp.async.bulk shared::cta -> shared::cluster), and each owner sums the C
 //              partials of its slice in rank order (deterministic) and stores it.
-// F8 variant (e4m3 weights with an fp32 scale per row): the ring holds 128-byte e4m3
-// rows (two k-blocks), warps 2-9 convert each k-block exactly to the 16-bit dtype
-// straight into TMEM (tcgen05.st), the MMA reads its A operand from TMEM, and the row
-// scale multiplies the k-summed value in the epilogue.
+// F8 variant (e4m3 weights with an fp32 scale per weight row): the ring holds 128-byte e4m3
+// rows (two k-blocks) that the MMA reads as they land (tcgen05.mma kind::f8f6f4, e4m3 x e4m3,
+// fp32 accumulate).  The normalised activations, formed exactly as on the 16-bit path, are
+// scaled per token by a power of two and split exactly into e4m3 terms (two for bf16, three
+// for fp16), so the k-summed products equal those of the 16-bit values; the epilogue undoes
+// the power of two and multiplies by the weight-row scale.
 // The host sizes (NT, C, STAGES) so that all clusters are resident at once
 // (cudaOccupancyMaxActiveClusters): a second wave would double the time.
 // Every wait is bounded (fqkv_device.cuh); after a timeout the kernel drains its own
@@ -37,8 +39,6 @@
 #include <map>
 #include <tuple>
 #include <type_traits>
-
-#include <cuda_fp8.h>
 
 #include "fqkv_kernels.cuh"
 
@@ -54,18 +54,17 @@ constexpr int kTileRows = 128;      // rows of W per MMA (UMMA M)
 constexpr int kKBlock = 64;         // K elements per stage (128 bytes of 16-bit data)
 constexpr int kWTileBytes = kTileRows * 128;
 // e4m3 weights: a ring tile is 128 rows of 128 one-byte elements (two 64-deep k-blocks, one
-// full 128-byte line per row), as many bytes as a 16-bit tile.
-constexpr int kW8Row = 128;
-// e4m3 weights: converted 16-bit A tiles in flight, in TMEM after the accumulators (32
-// columns each: 128 rows x 64 values): at most 5 * 32 + 8 * 32 = 416 of 512 columns.
-constexpr int kConvSlots = 8;
-__host__ __device__ constexpr int a_col_base(int nt, int mpad) { return (nt * mpad + 31) / 32 * 32; }
+// full 128-byte line per row), as many bytes as a 16-bit tile.  The activations' e4m3 terms
+// take one MPAD x 128-byte region each per two k-blocks.
+constexpr int kF8Batch = 8;                   // e4m3 weights: 16-byte chunks per lane and row in pass 2
+constexpr int kF8Max = kF8Batch * 32 / 8;     // k-blocks of one CTA's K slice at most (pass 2 in registers)
+__host__ __device__ constexpr int f8_terms(bool bf16) { return decode_f8_terms(bf16); }
 constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
 constexpr int kGridBatch = 8;       // grid variant: 16-byte chunks per thread loaded before any is used
 constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
 
 struct Layout {
-  uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, recvd, bars, tmem_slot, total;
+  uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, rscale, recvd, bars, tmem_slot, total;
 };
 
 // Receive slots of the cluster epilogue: in the ring after the partial tile (0), in the
@@ -78,76 +77,28 @@ __host__ __device__ constexpr uint32_t recv_own_bytes(int nt, int mpad) {
   return (uint32_t)(nt * mpad + kMaxCluster) * 128 * 4;
 }
 
-// f8: the ring holds e4m3 tiles (128-byte rows of two k-blocks, 128-byte swizzle); the
-// converted tiles live in TMEM.
-__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max, bool f8 = false,
+// f8 (the e4m3 terms of each activation, 0 for 16-bit weights): the ring holds e4m3 tiles
+// (128-byte rows of two k-blocks, 128-byte swizzle); the activation buffer holds f8 regions
+// of mpad x 128 bytes per two k-blocks (at least the 16-bit buffer the norm's first pass
+// fills).
+__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max, int f8 = 0,
                                               int recv_mode = kRecvRing) {
   Layout L;
   L.stage_bytes = nt * kWTileBytes;
   L.ring = 0;
   L.normed = L.ring + stages * L.stage_bytes;  // 1024-aligned: stages are multiples of 16 KB
-  L.gain = L.normed + (uint32_t)nkb_max * mpad * 128;  // [nkb_max * 64] fp32 gain slice
+  const int act_regions = f8 ? (nkb_max + 1) / 2 * f8 : nkb_max;
+  L.gain = L.normed + (uint32_t)act_regions * mpad * 128;  // [nkb_max * 64] fp32 gain slice
   L.red = L.gain + (uint32_t)nkb_max * kKBlock * 4;    // [kMaxCluster][mpad] floats
   L.rowp = L.red + kMaxCluster * mpad * 4;            // [mpad] floats
   L.rstd = L.rowp + mpad * 4;                         // [mpad] floats
-  L.recvd = (L.rstd + mpad * 4 + 15) & ~15u;          // kRecvOwn: the C receive slots
+  L.rscale = L.rstd + mpad * 4;                       // f8: [mpad] 2^-s of each token's terms
+  L.recvd = (L.rscale + mpad * 4 + 15) & ~15u;        // kRecvOwn: the C receive slots
   L.bars = (L.recvd + (recv_mode == kRecvOwn ? recv_own_bytes(nt, mpad) : 0u) + 7) & ~7u;
   // bars: full[S], empty[S], accum, normed, sum, part, acts, recv
-  L.tmem_slot = L.bars + (2 * stages + 6 + (f8 ? 2 * kConvSlots : 0)) * 8;  // + cfull, cempty
+  L.tmem_slot = L.bars + (2 * stages + 6) * 8;
   L.total = L.tmem_slot + 16;
   return L;
-}
-
-// Two e4m3 values -- bytes 0 and 1 of `w` (sel 0x1404) or bytes 2 and 3 (sel 0x3424) -- as
-// two values of the dtype, the lower byte in the lower half.  The byte permute places each
-// byte in the high byte of its 16-bit half; the shift puts the e4m3 exponent and mantissa
-// bits into the low end of the target's exponent field and the top of its mantissa (the
-// sign stays at bit 15), and the packed multiply by 2^(target bias - 7) -- 2^120 for bf16,
-// 2^8 for fp16 -- rescales.  Normal and subnormal e4m3 values come out exact (an e4m3
-// subnormal becomes a subnormal of the target before the multiply).  The e4m3fn NaN
-// encodings are read as +-480; quantize_weight_e4m3 never produces them.
-template <typename T>
-__device__ __forceinline__ uint32_t e4m3x2_to(uint32_t w, uint32_t sel);
-template <>
-__device__ __forceinline__ uint32_t e4m3x2_to<__half>(uint32_t w, uint32_t sel) {
-  const uint32_t x = __byte_perm(w, 0u, sel);
-  const uint32_t bits = (x & 0x80008000u) | ((x >> 1) & 0x3F803F80u);
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(0x5C005C00u));  // 2^8
-  return r;
-}
-template <>
-__device__ __forceinline__ uint32_t e4m3x2_to<__nv_bfloat16>(uint32_t w, uint32_t sel) {
-  const uint32_t x = __byte_perm(w, 0u, sel);
-  const uint32_t bits = (x & 0x80008000u) | ((x >> 4) & 0x07F007F0u);
-  uint32_t r;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(0x7B807B80u));  // 2^120
-  return r;
-}
-
-// A warp's share of one 128 x 64 k-block of e4m3 weights, converted into TMEM: rows
-// 32q .. 32q + 31 (q = warp % 4, the lane quadrant the warp may access; lane = row) and
-// values 32 hf .. 32 hf + 31 of the k-block (hf = which of the quadrant's two warps).  The
-// ring row is 128 bytes (two k-blocks, 128-byte swizzle: 16-byte chunk j at j ^ (row % 8)),
-// `h` picks the k-block.  Each lane converts its 32 values into 16 columns of the A slot.
-template <typename T>
-__device__ __forceinline__ void convert_w8_to_tmem(const uint8_t* tile, int h, int q, int hf, int lane,
-                                                   uint32_t a_taddr) {
-  const int r = q * 32 + lane;
-  const uint8_t* row = tile + r * kW8Row;
-  uint32_t o[16];
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int j = 4 * h + 2 * hf + u;  // logical 16-byte chunk of the row
-    const uint4 raw = *reinterpret_cast<const uint4*>(row + ((j ^ (r & 7)) << 4));
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      o[8 * u + 2 * v] = e4m3x2_to<T>(w[v], 0x1404u);
-      o[8 * u + 2 * v + 1] = e4m3x2_to<T>(w[v], 0x3424u);
-    }
-  }
-  tmem_st16(a_taddr + ((uint32_t)(q * 32) << 16) + 16 * hf, o);
 }
 
 // dtype(dtype(a * c) + dtype(b * s)): PyTorch's a * c + b * s on 16-bit tensors, the rounding
@@ -169,7 +120,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   FQKV_TRACE_DECL
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = make_layout(stages, NT, MPAD, p.nkb_max, F8, p.recv_in_normed);
+  const Layout L = make_layout(stages, NT, MPAD, p.nkb_max, F8 ? f8_terms(std::is_same<T, __nv_bfloat16>::value) : 0,
+                               p.recv_in_normed);
   uint8_t* ring = smem + L.ring;
   uint8_t* normed = smem + L.normed;
   float* red = reinterpret_cast<float*>(smem + L.red);
@@ -183,8 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* part_bar = accum_bar + 3;  // every CTA of the cluster has written its partial tile
   uint64_t* acts_bar = accum_bar + 4;  // the norm warps have issued their activation loads
   uint64_t* recv_bar = accum_bar + 5;  // the peers' slices of this CTA's share have landed
-  uint64_t* cfull = accum_bar + 6;     // e4m3 weights: conversion slot filled (8 warps)
-  uint64_t* cempty = cfull + kConvSlots;  // e4m3 weights: conversion slot consumed (MMA commit)
+  float* rscale = reinterpret_cast<float*>(smem + L.rscale);
   float* gain_s = reinterpret_cast<float*>(smem + L.gain);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   // The epilogue reuses buffers the MMAs no longer need: this CTA's partial tile
@@ -209,9 +160,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb0 = (int)((rank * (uint32_t)KB) / C), kb1 = (int)(((rank + 1) * (uint32_t)KB) / C);
   const int nkb = kb1 - kb0;
   const int n_base = blockIdx.y * NT * kTileRows;
-  // Accumulators [0, NT * MPAD); e4m3 weights: kConvSlots A tiles of 32 columns after them.
-  constexpr uint32_t kACol = a_col_base(NT, MPAD);
-  constexpr uint32_t kTmemCols = tmem_cols_for(F8 ? kACol + kConvSlots * 32 : NT * MPAD);
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int kTerms = F8 ? f8_terms(kBF16) : 1;  // e4m3: terms of each activation, stacked along N
+  // Accumulators [0, NT * kTerms * MPAD): tile nt's term t in columns (nt * kTerms + t) * MPAD.
+  constexpr uint32_t kTmemCols = tmem_cols_for(NT * kTerms * MPAD);
   constexpr int kBoxTiles = decode_box_tiles(NT);
 
   // ---------------------------------------------------------------- setup
@@ -219,13 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], F8 ? kNormWarps : 1);  // e4m3: freed by the converting warps
-    }
-    if (F8) {
-      for (int i = 0; i < kConvSlots; ++i) {
-        mbar_init(&cfull[i], kNormWarps);
-        mbar_init(&cempty[i], 1);
-      }
+      mbar_init(&empty[s], 1);
     }
     mbar_init(accum_bar, 1);
     mbar_init(normed_bar, 1);
@@ -292,41 +238,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16(kTileRows, MPAD, std::is_same<T, __nv_bfloat16>::value);
+      const uint32_t idesc = F8 ? make_idesc_f8(kTileRows, kTerms * MPAD) : make_idesc_f16(kTileRows, MPAD, kBF16);
       bool ok = mbar_wait(normed_bar, 0);
       int s = 0, round = 0;
-      if (F8) {
-        // e4m3 weights: each 128-row tile arrives converted in a slot of its own.
-        for (int i = 0; i < nkb && ok; ++i) {
-          const uint32_t b_base = smem_u32(normed + i * MPAD * 128);
-#pragma unroll 1
-          for (int nt = 0; nt < NT; ++nt) {
-            const int task = i * NT + nt, slot = task % kConvSlots;
-            if (!(ok = mbar_spin(&cfull[slot], (task / kConvSlots) & 1))) break;
-            tc_fence_after();
-            const uint32_t a_tmem = tmem_base + kACol + slot * 32;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_f16_ts(tmem_base + nt * MPAD, a_tmem + kk * 8, make_sw128_desc(b_base + kk * 32), idesc,
-                          (i > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(&cempty[slot]);
-          }
-        }
-      }
-      for (int i = 0; i < (F8 ? 0 : nkb) && ok; ++i) {
+      for (int i = 0; i < nstage && ok; ++i) {
         if (!(ok = mbar_wait(&full[s], round & 1))) break;
         if (i == 0) FQKV_TRACE_POINT(11);
-        if (i == nkb - 1) FQKV_TRACE_POINT(12);
+        if (i == nstage - 1) FQKV_TRACE_POINT(12);
         tc_fence_after();
         const uint32_t a_base = smem_u32(ring + s * L.stage_bytes);
-        const uint32_t b_base = smem_u32(normed + i * MPAD * 128);
+        if (F8) {
+          // e4m3: one stage is 128 K (two k-blocks); each 32-byte step is one MMA whose B
+          // operand is the kTerms x MPAD rows of the terms' regions (contiguous), so the
+          // terms' products land in kTerms column blocks of the tile's accumulator.
+          const uint32_t b_base = smem_u32(normed + i * kTerms * MPAD * 128);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t bdesc = make_sw128_desc(b_base + kk * 32);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bdesc = make_sw128_desc(b_base + kk * 32);
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const uint64_t adesc = make_sw128_desc(a_base + nt * kWTileBytes + kk * 32);
-            umma_f16(tmem_base + nt * MPAD, adesc, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint64_t adesc = make_sw128_desc(a_base + nt * kWTileBytes + kk * 32);
+              umma_f8(tmem_base + nt * kTerms * MPAD, adesc, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+        } else {
+          const uint32_t b_base = smem_u32(normed + i * MPAD * 128);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bdesc = make_sw128_desc(b_base + kk * 32);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint64_t adesc = make_sw128_desc(a_base + nt * kWTileBytes + kk * 32);
+              umma_f16(tmem_base + nt * MPAD, adesc, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
         }
         umma_commit(&empty[s]);
@@ -566,7 +510,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       g2[2] = c.x;
       g2[3] = c.y;
     };
-    if (h_in_regs) {
+    if (F8) {
+      // e4m3 weights: per token row (one warp each), the normalised values -- exactly the
+      // 16-bit path's -- times 2^s, with 2^s putting the row's largest magnitude in
+      // [128, 256), split exactly into kTerms e4m3 terms (each the rounding of what the
+      // earlier ones left); 2^-s goes to the epilogue.  The terms of every 128 K (two
+      // k-blocks) fill kTerms regions of MPAD x 128 bytes, zeros beyond the slice and for
+      // rows >= M.  Each warp reads all of its row before writing it (in place).
+      const int nchunk16 = (nchunk + 15) & ~15;  // 16-byte chunks rounded up to whole 128 K
+      // chunk j of row m: 8 values at byte 8 (j % 16) of the row's 128-byte line in the
+      // terms' regions (j / 16) * kTerms + t
+      auto term_off = [&](int m, int j) {
+        return (uint32_t)((j >> 4) * kTerms) * (MPAD * 128) + (uint32_t)m * 128u +
+               ((((uint32_t)(j & 15) >> 1) ^ ((uint32_t)m & 7u)) << 4) + ((uint32_t)(j & 1) << 3);
+      };
+      for (int mb = nw; mb < MPAD; mb += 2 * kNormWarps)  // rows in pass 1's pairs (register slot q2)
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int m0 = mb + kNormWarps * q2;
+          if (m0 >= p.M) {  // padding rows: zero terms
+            for (int j = lane; j < nchunk16; j += 32)
+#pragma unroll
+              for (int t = 0; t < kTerms; ++t)
+                *reinterpret_cast<uint2*>(normed + term_off(m0, j) + t * (MPAD * 128)) = make_uint2(0u, 0u);
+            if (lane == 0) rscale[m0] = 0.f;
+            continue;
+          }
+          const float rs = rstd_s[m0];
+          const uint64_t rs2 = f2_pack(rs, rs);
+          uint4 o[kF8Batch];
+          uint32_t mx2 = 0u;
+#pragma unroll
+          for (int b = 0; b < kF8Batch; ++b) {
+            const int j = lane + 32 * b;
+            o[b] = make_uint4(0, 0, 0, 0);
+            if (j < nchunk && k_lo + (int64_t)j * 8 < p.H) {
+              // h_in_regs holds at most 32 * kLoadBatch chunks, so b < kLoadBatch there
+              const uint4 hv = (h_in_regs && b < kLoadBatch)
+                                   ? hkeep[q2][b < kLoadBatch ? b : 0]
+                                   : *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) +
+                                                                     sw128_offset(m0, j & 7));
+              uint64_t g2[4];
+              load_g2(j, g2);
+              o[b] = normalize8_f2<T>(hv, rs2, g2);
+              mx2 = absmax8_bits(o[b], mx2);
+            }
+          }
+          const uint32_t mxb = __reduce_max_sync(0xffffffffu, max(mx2 & 0xFFFFu, mx2 >> 16));
+          const float mx = Elem<T>::to_f((uint16_t)mxb);
+          // mx in [2^e, 2^(e+1)): scale by 2^(7 - e).
+          const int e = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127 : 7;
+          const int sh = min(max(7 - e, -100), 100);
+          const float up = __uint_as_float((uint32_t)(127 + sh) << 23);
+          if (lane == 0) rscale[m0] = __uint_as_float((uint32_t)(127 - sh) << 23);
+          __syncwarp();  // every lane has read its row before any lane writes the terms over it
+#pragma unroll
+          for (int b = 0; b < kF8Batch; ++b) {
+            const int j = lane + 32 * b;
+            if (j < nchunk16) {
+              uint2 t8[kTerms];
+              split_e4m3<T, kTerms>(o[b], up, t8);
+#pragma unroll
+              for (int t = 0; t < kTerms; ++t)
+                *reinterpret_cast<uint2*>(normed + term_off(m0, j) + t * (MPAD * 128)) = t8[t];
+            }
+          }
+        }
+    } else if (h_in_regs) {
       uint64_t rs2[2];
 #pragma unroll
       for (int q2 = 0; q2 < 2; ++q2) {
@@ -620,36 +630,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // bounded wait runs out; it then commits no MMA and the kernel winds down as usual.
     if (et == 0 && !(p.flags & FQKV_FLAG_TEST_WITHHOLD)) mbar_arrive(normed_bar);
     if (et == 0) FQKV_TRACE_POINT(10);
-
-    if (F8) {
-      // e4m3 weights: convert stage s of the ring tile by tile into the conversion slots
-      // the MMA reads.  Each warp converts its rows of every tile and waits on its own (no
-      // named barrier in this loop: a warp whose bounded wait gives up leaves early, and
-      // every warp still meets the epilogue's barriers the same number of times).
-      bool wok = ok;
-      for (int js = 0; 2 * js < nkb && wok; ++js) {  // ring stage js: k-blocks 2 js, 2 js + 1
-        const int s = js % stages;
-        wok = __all_sync(0xffffffffu, mbar_wait(&full[s], (js / stages) & 1));
-        for (int h = 0; h < 2 && 2 * js + h < nkb && wok; ++h) {
-          const int i = 2 * js + h;
-          for (int nt = 0; nt < NT && wok; ++nt) {
-            const int task = i * NT + nt, slot = task % kConvSlots;
-            if (task >= kConvSlots)
-              wok = __all_sync(0xffffffffu, mbar_spin(&cempty[slot], (task / kConvSlots - 1) & 1));
-            if (!wok) break;
-            convert_w8_to_tmem<T>(ring + s * L.stage_bytes + nt * kWTileBytes, h, warp & 3, (warp - 2) >> 2, lane,
-                                  tmem_base + kACol + slot * 32);
-            tmem_wait_st();
-            tc_fence_before();  // the MMA thread reads the slot after the arrive below
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&cfull[slot]);
-          }
-        }
-        __syncwarp();
-        if (wok && lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
-      }
-      ok = bar_and(1, kNormThreads, wok) && ok;  // every warp has left the loop
-    }
 
     ok = mbar_wait(accum_bar, 0) && ok;
     if (et == 0) FQKV_TRACE_POINT(13);
@@ -734,11 +714,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c0 = 0; c0 < MPAD; c0 += 16) {
           if (((nt * (MPAD / 16) + c0 / 16) & 1) != half) continue;
-          uint32_t v[16];
-          tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + nt * MPAD + c0, v);
+          uint32_t v[kTerms][16];
+#pragma unroll
+          for (int t = 0; t < kTerms; ++t)
+            tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (nt * kTerms + t) * MPAD + c0, v[t]);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) part[((c0 + e) * NT + nt) * kTileRows + row] = __uint_as_float(v[e]);
+          for (int e = 0; e < 16; ++e) {
+            // e4m3: the terms' sums in term order, then the token's power of two undone (exact)
+            float a = __uint_as_float(v[0][e]);
+#pragma unroll
+            for (int t = 1; t < kTerms; ++t) a += __uint_as_float(v[t][e]);
+            part[((c0 + e) * NT + nt) * kTileRows + row] = F8 ? a * rscale[c0 + e] : a;
+          }
         }
       }
       tc_fence_before();
@@ -947,14 +935,14 @@ constexpr size_t kSmemLimit = 232448;  // max dynamic shared memory per block on
 
 size_t decode_smem_bytes(const DecodeConfig& c, int kb_total) {
   const int nkb_max = (kb_total + c.cluster - 1) / c.cluster;
-  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8 != 0, c.recv_in_normed).total;
+  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8, c.recv_in_normed).total;
 }
 
 // Choose (tile rows, cluster size, ring depth).  Candidates must fit shared memory and
 // have every cluster resident at once; among them the one using the most SMs wins (ties
 // go to the deeper ring, then to the smaller cluster).
 // FQKV_DECODE_NT / FQKV_DECODE_CLUSTER / FQKV_DECODE_STAGES restrict the search.
-int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, bool f8) {
+int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, int f8) {
   const int mpad = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
   if (mpad == 0) return FQKV_ERR_SCHEDULE;
   // Tuning overrides, read once per process.
@@ -974,7 +962,7 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, boo
   int dev = 0;
   cudaGetDevice(&dev);
   const auto key = std::make_tuple(dev, mpad, H, N, sm_count, force_nt, force_c, force_s * 4 + recv_mode_env,
-                                   f8 ? 1 : 0);
+                                   f8);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -988,12 +976,16 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, boo
   long best_score = -1;
   for (int nt = 1; nt <= kMaxNT; ++nt) {
     if (force_nt && nt != force_nt) continue;
-    if (!pick_kernel(mpad, nt, true, f8)) continue;
+    if (!pick_kernel(mpad, nt, true, f8 != 0)) continue;
+    // TMEM: at most half an SM's 512 columns, so that two CTAs of a cluster placed on one SM
+    // could always both allocate (each waits in tcgen05.alloc for the other otherwise).
+    if (tmem_cols_for(nt * std::max(f8, 1) * mpad) > 256) continue;
     const int tile_bytes = kWTileBytes;  // one 128-row tile in the ring (e4m3: two k-blocks)
     const int tiles = (N + nt * kTileRows - 1) / (nt * kTileRows);
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
       if ((KB + cl - 1) / cl * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
+      if (f8 && (KB + cl - 1) / cl > kF8Max) continue;  // e4m3: the slice's terms formed in registers
       // The epilogue's partial tile aliases the ring.  Its C receive slots get a region of
       // their own (16-bit weights, up to 32 rows) when that still leaves a ring of three
       // stages or more; otherwise they go into the normalised-activation buffer when they fit
@@ -1007,16 +999,16 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, boo
         const int min_stages = (epi_bytes + nt * tile_bytes - 1) / (nt * tile_bytes);
         for (int st = 16; st >= max(2, min_stages); --st) {
           if (force_s && st != force_s) continue;
-          DecodeConfig t{mpad, nt, st, cl, 0, mode, f8 ? 1 : 0};
+          DecodeConfig t{mpad, nt, st, cl, 0, mode, f8};
           t.smem = decode_smem_bytes(t, KB);
           if (t.smem > kSmemLimit) continue;
           if (max_active_clusters(t, tiles) < tiles) continue;  // would need a second wave
           return t;
         }
-        return DecodeConfig{mpad, nt, 0, cl, 0, mode, f8 ? 1 : 0};
+        return DecodeConfig{mpad, nt, 0, cl, 0, mode, f8};
       };
       DecodeConfig t = deepest(alias_mode);
-      if (recv_mode_env != 1 && !f8 && mpad <= 32) {
+      if (recv_mode_env != 1 && mpad <= 32) {
         const DecodeConfig own = deepest(kRecvOwn);
         if (own.stages >= 3 || (own.stages > 0 && t.stages == 0)) t = own;
       }

@@ -217,6 +217,60 @@ __device__ __forceinline__ uint4 normalize8_f2(uint4 h, uint64_t rs2, const uint
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Largest magnitude of 8 elements as its 16-bit pattern: fp16 and bf16 magnitudes order like
+// their bit patterns with the sign cleared, so a packed unsigned max of (bits & 0x7FFF)
+// finds it (a NaN's pattern is above every finite value's).
+__device__ __forceinline__ uint32_t absmax8_bits(uint4 v, uint32_t m2) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) asm("max.u16x2 %0, %0, %1;" : "+r"(m2) : "r"(w[i] & 0x7FFF7FFFu));
+  return m2;
+}
+
+// Two elements of a 16-bit word times `up` (a power of two), as an f16x2 word: exact for
+// every product of 2^-17 or more in magnitude (8 or 11 significant bits), and the products
+// are below 256.  What is smaller lies below half of e4m3's smallest subnormal (2^-10) and
+// adds no e4m3 term either way.
+template <typename T>
+__device__ __forceinline__ uint32_t scaled_f16x2(uint32_t w, float up) {
+  const float lo = Elem<T>::to_f((uint16_t)(w & 0xFFFFu)) * up;
+  const float hi = Elem<T>::to_f((uint16_t)(w >> 16)) * up;
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// 8 elements times `up` (a power of two) as K e4m3 terms, one 8-byte group each (element e
+// in byte e): term t is the value left by terms 0 .. t-1, rounded to e4m3 (the hardware
+// conversion, round to nearest even, saturating).  The values and what is left stay in
+// f16x2 words: each difference of a value and its e4m3 rounding is exact there.  With
+// |value * up| < 256, two terms hold a bf16 value and three an fp16 value exactly, but for
+// what falls below e4m3's smallest subnormal, 2^-9 (values 2^16 times below the row's
+// largest and smaller).
+template <typename T, int K>
+__device__ __forceinline__ void split_e4m3(uint4 v, float up, uint2 (&out)[K]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r[i] = scaled_f16x2<T>(w[i], up);
+#pragma unroll
+  for (int t = 0; t < K; ++t) {
+    uint32_t b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint16_t q;
+      asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(q) : "r"(r[i]));
+      b[i] = q;
+      if (t + 1 < K) {
+        uint32_t back;
+        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(back) : "h"(q));
+        asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(r[i]) : "r"(back));
+      }
+    }
+    out[t] = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+  }
+}
+
 // ss + sum of squares of the 8 elements, in element order.
 template <typename T>
 __device__ __forceinline__ float sumsq8_acc(uint4 v, float ss) {
@@ -338,12 +392,16 @@ struct DecodeConfig {
   int cluster;  // CTAs splitting K (cluster size)
   size_t smem;  // dynamic shared memory bytes
   int recv_in_normed;  // see DecodeParams
-  int f8;       // e4m3 weights (converted to the dtype in shared memory before the MMA)
+  int f8;       // e4m3 weights: the e4m3 terms each activation is split into (2 for bf16,
+                // 3 for fp16); 0 for 16-bit weights
   int grid;     // 1: `cluster` independent CTAs split K (no cluster); they sum their partial
                 // tiles through the workspace
 };
 
-int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, bool f8 = false);
+// e4m3 terms that hold a normalised 16-bit activation exactly (8 or 11 significant bits).
+__host__ __device__ constexpr int decode_f8_terms(bool bf16) { return bf16 ? 2 : 3; }
+// f8: 0 for 16-bit weights, else decode_f8_terms of the activation dtype.
+int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, int f8 = 0);
 // DecodeConfig::recv_in_normed value of the receive slots in a region of their own (the
 // epilogue needs no cluster agreement before its copies; the rotary split needs these).
 constexpr int kDecodeRecvOwn = 2;
