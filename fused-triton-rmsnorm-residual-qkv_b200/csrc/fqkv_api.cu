@@ -373,7 +373,7 @@ extern "C" FQKV_API int fqkv_launch_fp8w(const void* x, const void* residual, co
   DecodeParams dp{static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(residual), rms_weight,
                   rms_weight_dtype, static_cast<uint16_t*>(out), static_cast<uint16_t*>(residual_out), (int)M,
                   (int)H, (int)N, ldx, ldr, ldo, ldro, eps, (int)((H + 63) / 64), 0, flags, 0, 0, weight_scale};
-  dp.nkb_max = (dp.kb_total + c.cluster - 1) / c.cluster;
+  dp.nkb_max = decode_slice_max(c.cluster, dp.kb_total, true);
   // Rings of two stages skip programmatic dependent launch (as on the 16-bit path; here at
   // every M: the N = 28672 configuration measured 65.9 us at M = 1 with it).
   const bool pdl = (flags & FQKV_FLAG_PDL) != 0 && c.stages > 2;

@@ -136,7 +136,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acts_bar = accum_bar + 4;  // the norm warps have issued their activation loads
   uint64_t* recv_bar = accum_bar + 5;  // the peers' slices of this CTA's share have landed
   float* rscale = reinterpret_cast<float*>(smem + L.rscale);
-  float* gain_s = reinterpret_cast<float*>(smem + L.gain);
+  // The gain slice as two arrays of 16-byte halves (elements 0-3 and 4-7 of each 8-element
+  // chunk), so that a warp's 16-byte loads of consecutive chunks hit every bank once.
+  float4* gain_lo = reinterpret_cast<float4*>(smem + L.gain);
+  float4* gain_hi = gain_lo + p.nkb_max * (kKBlock / 8);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   // The epilogue reuses buffers the MMAs no longer need: this CTA's partial tile
   // [MPAD][NT][128] floats at the start of the ring, and C receive slots for the peers'
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(kNormWarps <= kMaxCluster, "the grid variant's per-warp row sums use the cluster sum slots");
   // Hand-offs wait by polling their mbarrier (test_wait) when p.poll, else in try_wait.
   const int KB = p.kb_total;
-  const int kb0 = (int)((rank * (uint32_t)KB) / C), kb1 = (int)(((rank + 1) * (uint32_t)KB) / C);
+  const int kb0 = decode_slice_begin((int)rank, (int)C, KB, F8), kb1 = decode_slice_begin((int)rank + 1, (int)C, KB, F8);
   const int nkb = kb1 - kb0;
   const int n_base = blockIdx.y * NT * kTileRows;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -445,7 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (write_res && live && j < nchunk && k < p.H)
                 *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
               hkeep[q2][b] = hv;
-              if (j < nchunk) *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
+              if (live && j < nchunk)
+                *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
             }
           }
         }
@@ -466,8 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j < nchunk) {
         float4 gv[2];
         gain_raw_to_f32(p.gdt, graw[i], gv);
-        reinterpret_cast<float4*>(gain_s)[2 * j] = gv[0];
-        reinterpret_cast<float4*>(gain_s)[2 * j + 1] = gv[1];
+        gain_lo[j] = gv[0];
+        gain_hi[j] = gv[1];
       }
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -503,20 +507,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Pass 2: normalise, dtype((h * rstd) * g), over pass 1's rows and chunks; a lane's gain
     // pairs for its kLoadBatch chunks are loaded once and serve all its rows.
     auto load_g2 = [&](int j, uint64_t (&g2)[4]) {
-      const ulonglong2 a = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j];
-      const ulonglong2 c = reinterpret_cast<const ulonglong2*>(gain_s)[2 * j + 1];
+      const ulonglong2 a = reinterpret_cast<const ulonglong2*>(gain_lo)[j];
+      const ulonglong2 c = reinterpret_cast<const ulonglong2*>(gain_hi)[j];
       g2[0] = a.x;
       g2[1] = a.y;
       g2[2] = c.x;
       g2[3] = c.y;
     };
     if (F8) {
-      // e4m3 weights: per token row (one warp each), the normalised values -- exactly the
-      // 16-bit path's -- times 2^s, with 2^s putting the row's largest magnitude in
-      // [128, 256), split exactly into kTerms e4m3 terms (each the rounding of what the
+      // e4m3 weights: per token row (a warp takes pass 1's pairs), the normalised values --
+      // exactly the 16-bit path's -- times 2^s, with 2^s putting the row's largest magnitude
+      // in [128, 256), split exactly into kTerms e4m3 terms (each the rounding of what the
       // earlier ones left); 2^-s goes to the epilogue.  The terms of every 128 K (two
-      // k-blocks) fill kTerms regions of MPAD x 128 bytes, zeros beyond the slice and for
-      // rows >= M.  Each warp reads all of its row before writing it (in place).
+      // k-blocks) fill kTerms regions of MPAD x 128 bytes, zeros beyond the slice.  Each warp
+      // reads all of its rows before writing them (in place).
       const int nchunk16 = (nchunk + 15) & ~15;  // 16-byte chunks rounded up to whole 128 K
       // chunk j of row m: 8 values at byte 8 (j % 16) of the row's 128-byte line in the
       // terms' regions (j / 16) * kTerms + t
@@ -524,76 +528,99 @@ __global__ void __launch_bounds__(kThreads, 1)
         return (uint32_t)((j >> 4) * kTerms) * (MPAD * 128) + (uint32_t)m * 128u +
                ((((uint32_t)(j & 15) >> 1) ^ ((uint32_t)m & 7u)) << 4) + ((uint32_t)(j & 1) << 3);
       };
-      for (int mb = nw; mb < MPAD; mb += 2 * kNormWarps)  // rows in pass 1's pairs (register slot q2)
-#pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int m0 = mb + kNormWarps * q2;
-          if (m0 >= p.M) {  // padding rows: zero terms
-            for (int j = lane; j < nchunk16; j += 32)
-#pragma unroll
-              for (int t = 0; t < kTerms; ++t)
-                *reinterpret_cast<uint2*>(normed + term_off(m0, j) + t * (MPAD * 128)) = make_uint2(0u, 0u);
-            if (lane == 0) rscale[m0] = 0.f;
-            continue;
-          }
-          const float rs = rstd_s[m0];
-          const uint64_t rs2 = f2_pack(rs, rs);
-          uint4 o[kF8Batch];
-          uint32_t mx2 = 0u;
-#pragma unroll
-          for (int b = 0; b < kF8Batch; ++b) {
-            const int j = lane + 32 * b;
-            o[b] = make_uint4(0, 0, 0, 0);
-            if (j < nchunk && k_lo + (int64_t)j * 8 < p.H) {
-              // h_in_regs holds at most 32 * kLoadBatch chunks, so b < kLoadBatch there
-              const uint4 hv = (h_in_regs && b < kLoadBatch)
-                                   ? hkeep[q2][b < kLoadBatch ? b : 0]
-                                   : *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) +
-                                                                     sw128_offset(m0, j & 7));
+      // NB 16-byte chunks per lane and row; kRegs: h is still in registers from pass 1.
+      auto pass2_f8 = [&](auto nb_c, auto regs_c) {
+        constexpr int NB = decltype(nb_c)::value;
+        constexpr bool kRegs = decltype(regs_c)::value;
+        for (int mb = nw; mb < p.M; mb += 2 * kNormWarps) {  // pass 1's row pairs (register slot q2)
+          // Rows mb and mb + 8 (live when < M; the padding rows' terms are never written: they
+          // reach only accumulator columns that are never read), both at once.
+          const bool live1 = mb + kNormWarps < p.M;
+          uint64_t rs2[2];
+          rs2[0] = f2_pack(rstd_s[mb], rstd_s[mb]);
+          rs2[1] = live1 ? f2_pack(rstd_s[mb + kNormWarps], rstd_s[mb + kNormWarps]) : 0ull;
+          uint4 o[2][NB];
+          uint32_t mx2[2] = {0u, 0u};
+  #pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            o[0][b] = o[1][b] = make_uint4(0, 0, 0, 0);
+            if (32 * b < nchunk) {  // warp-uniform
+              const int j = lane + 32 * b;
+              const bool in = j < nchunk && k_lo + (int64_t)j * 8 < p.H;
               uint64_t g2[4];
-              load_g2(j, g2);
-              o[b] = normalize8_f2<T>(hv, rs2, g2);
-              mx2 = absmax8_bits(o[b], mx2);
+              load_g2(j < nchunk ? j : nchunk - 1, g2);  // clamped: always inside the gain slice
+  #pragma unroll
+              for (int q2 = 0; q2 < 2; ++q2) {
+                if (q2 == 1 && !live1) continue;
+                const int m0 = mb + kNormWarps * q2;
+                uint4 hv = make_uint4(0, 0, 0, 0);
+                if constexpr (kRegs)
+                  hv = hkeep[q2][b];
+                else if (in)
+                  hv = *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m0, j & 7));
+                if (in) {
+                  o[q2][b] = normalize8_f2<T>(hv, rs2[q2], g2);
+                  mx2[q2] = absmax8_bits(o[q2][b], mx2[q2]);
+                }
+              }
             }
           }
-          const uint32_t mxb = __reduce_max_sync(0xffffffffu, max(mx2 & 0xFFFFu, mx2 >> 16));
-          const float mx = Elem<T>::to_f((uint16_t)mxb);
-          // mx in [2^e, 2^(e+1)): scale by 2^(7 - e).
-          const int e = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127 : 7;
-          const int sh = min(max(7 - e, -100), 100);
-          const float up = __uint_as_float((uint32_t)(127 + sh) << 23);
-          if (lane == 0) rscale[m0] = __uint_as_float((uint32_t)(127 - sh) << 23);
-          __syncwarp();  // every lane has read its row before any lane writes the terms over it
-#pragma unroll
-          for (int b = 0; b < kF8Batch; ++b) {
+          float up[2] = {0.f, 0.f};
+  #pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            if (q2 == 1 && !live1) continue;
+            const uint32_t mxb = __reduce_max_sync(0xffffffffu, max(mx2[q2] & 0xFFFFu, mx2[q2] >> 16));
+            const float mx = Elem<T>::to_f((uint16_t)mxb);
+            // mx in [2^e, 2^(e+1)): scale by 2^(7 - e).
+            const int e = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127 : 7;
+            const int sh = min(max(7 - e, -100), 100);
+            up[q2] = __uint_as_float((uint32_t)(127 + sh) << 23);
+            if (lane == 0) rscale[mb + kNormWarps * q2] = __uint_as_float((uint32_t)(127 - sh) << 23);
+          }
+          if (et == 0) FQKV_TRACE_POINT(19);
+          __syncwarp();  // every lane has read its rows before any lane writes the terms over them
+  #pragma unroll
+          for (int b = 0; b < NB; ++b) {
             const int j = lane + 32 * b;
-            if (j < nchunk16) {
-              uint2 t8[kTerms];
-              split_e4m3<T, kTerms>(o[b], up, t8);
-#pragma unroll
-              for (int t = 0; t < kTerms; ++t)
-                *reinterpret_cast<uint2*>(normed + term_off(m0, j) + t * (MPAD * 128)) = t8[t];
+            if (32 * b < nchunk16 && j < nchunk16) {
+  #pragma unroll
+              for (int q2 = 0; q2 < 2; ++q2) {
+                if (q2 == 1 && !live1) continue;
+                const int m0 = mb + kNormWarps * q2;
+                uint2 t8[kTerms];
+                split_e4m3<T, kTerms>(o[q2][b], up[q2], t8);
+  #pragma unroll
+                for (int t = 0; t < kTerms; ++t)
+                  *reinterpret_cast<uint2*>(normed + term_off(m0, j) + t * (MPAD * 128)) = t8[t];
+              }
             }
           }
         }
+      };
+      if (h_in_regs)
+        pass2_f8(std::integral_constant<int, kLoadBatch>{}, std::true_type{});
+      else
+        pass2_f8(std::integral_constant<int, kF8Batch>{}, std::false_type{});
     } else if (h_in_regs) {
-      uint64_t rs2[2];
+      if (nw < p.M) {  // rows nw and nw + 8; padding rows are skipped (warp-uniform)
+        const bool live1 = nw + kNormWarps < p.M;
+        uint64_t rs2[2];
+        rs2[0] = f2_pack(rstd_s[nw], rstd_s[nw]);
+        rs2[1] = live1 ? f2_pack(rstd_s[nw + kNormWarps], rstd_s[nw + kNormWarps]) : 0ull;
 #pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        const float rs = rstd_s[nw + kNormWarps * q2];
-        rs2[q2] = f2_pack(rs, rs);
-      }
+        for (int b = 0; b < kLoadBatch; ++b) {
+          if (32 * b >= nchunk) continue;  // warp-uniform
+          const int j = lane + 32 * b;
+          const bool in = j < nchunk && k_lo + (int64_t)j * 8 < p.H;
+          uint64_t g2[4];
+          load_g2(j < nchunk ? j : nchunk - 1, g2);  // clamped: always inside the gain slice
 #pragma unroll
-      for (int b = 0; b < kLoadBatch; ++b) {
-        const int j = lane + 32 * b;
-        const bool in = j < nchunk && k_lo + (int64_t)j * 8 < p.H;
-        uint64_t g2[4];
-        load_g2(j < nchunk ? j : nchunk - 1, g2);  // clamped: always inside the gain slice
-#pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int m = nw + kNormWarps * q2;
-          const uint4 o = normalize8_f2<T>(hkeep[q2][b], rs2[q2], g2);
-          if (in && m < p.M) *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = o;
+          for (int q2 = 0; q2 < 2; ++q2) {
+            if (q2 == 1 && !live1) continue;
+            const int m = nw + kNormWarps * q2;
+            const uint4 o = normalize8_f2<T>(hkeep[q2][b], rs2[q2], g2);
+            if (in) *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = o;
+          }
         }
       }
     } else {
@@ -624,6 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (et == 0) FQKV_TRACE_POINT(20);
     fence_proxy_async_smem();
     asm volatile("bar.sync 1, 256;" ::: "memory");
     // FQKV_FLAG_TEST_WITHHOLD (tests of the failure path): no arrival, so the MMA thread's
@@ -934,7 +962,7 @@ int env_int(const char* name, int dflt) {
 constexpr size_t kSmemLimit = 232448;  // max dynamic shared memory per block on sm_100
 
 size_t decode_smem_bytes(const DecodeConfig& c, int kb_total) {
-  const int nkb_max = (kb_total + c.cluster - 1) / c.cluster;
+  const int nkb_max = decode_slice_max(c.cluster, kb_total, c.f8 != 0);
   return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8, c.recv_in_normed).total;
 }
 
@@ -984,15 +1012,17 @@ int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, int
     const int tiles = (N + nt * kTileRows - 1) / (nt * kTileRows);
     for (int cl = 1; cl <= kMaxCluster && cl <= KB; ++cl) {
       if (force_c && cl != force_c) continue;
-      if ((KB + cl - 1) / cl * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
-      if (f8 && (KB + cl - 1) / cl > kF8Max) continue;  // e4m3: the slice's terms formed in registers
+      if (f8 && cl > (KB + 1) / 2) continue;  // every CTA gets one e4m3 stage at least
+      const int nkb_max = decode_slice_max(cl, KB, f8 != 0);
+      if (nkb_max * 8 > kGainChunks * kNormThreads) continue;  // gain slice held in registers
+      if (f8 && nkb_max > kF8Max) continue;  // e4m3: the slice's terms formed in registers
       // The epilogue's partial tile aliases the ring.  Its C receive slots get a region of
       // their own (16-bit weights, up to 32 rows) when that still leaves a ring of three
       // stages or more; otherwise they go into the normalised-activation buffer when they fit
       // there, else after the partial tile in the ring.
       const int part_bytes = nt * mpad * kTileRows * 4;
       const int recv_bytes = cl * 16 * ((nt * mpad * (kTileRows / 4) + cl - 1) / cl);
-      const int alias_mode = recv_bytes <= (KB + cl - 1) / cl * mpad * 128 ? kRecvNormed : kRecvRing;
+      const int alias_mode = recv_bytes <= nkb_max * mpad * 128 ? kRecvNormed : kRecvRing;
       // Deepest resident ring of a receive mode for this (nt, cl), or a config with stages 0.
       auto deepest = [&](int mode) {
         const int epi_bytes = part_bytes + (mode == kRecvRing ? recv_bytes : 0);

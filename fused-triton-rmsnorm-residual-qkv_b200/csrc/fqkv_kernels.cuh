@@ -400,6 +400,15 @@ struct DecodeConfig {
 
 // e4m3 terms that hold a normalised 16-bit activation exactly (8 or 11 significant bits).
 __host__ __device__ constexpr int decode_f8_terms(bool bf16) { return bf16 ? 2 : 3; }
+// The K slice of rank r of the C CTAs splitting KB 64-deep k-blocks: [begin(r), begin(r + 1)).
+// e4m3 weights split in units of two k-blocks (one ring stage of 128 one-byte columns), so
+// that no CTA streams a half-empty stage.
+__host__ __device__ constexpr int decode_slice_begin(int r, int C, int KB, bool f8) {
+  return f8 ? (2 * ((r * ((KB + 1) / 2)) / C) < KB ? 2 * ((r * ((KB + 1) / 2)) / C) : KB) : (r * KB) / C;
+}
+__host__ __device__ constexpr int decode_slice_max(int C, int KB, bool f8) {
+  return f8 ? 2 * (((KB + 1) / 2 + C - 1) / C) : (KB + C - 1) / C;
+}
 // f8: 0 for 16-bit weights, else decode_f8_terms of the activation dtype.
 int decode_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg, int f8 = 0);
 // DecodeConfig::recv_in_normed value of the receive slots in a region of their own (the
