@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // f = ((m * NT + nt) * 128 + row) / 4 for token m < M; rank o reduces [F(o), F(o+1)).
     // With the rotary split, shares are whole 128-row blocks (m, nt): a head's two halves stay
     // with one CTA.
-    const bool rope = p.q != nullptr;
+    const bool rope = !F8 && !GRID && p.q != nullptr;  // the rotary split: 16-bit weights, cluster kernel
     const uint32_t total4 = (uint32_t)(NT * p.M * (kTileRows / 4));
     auto share = [&](uint32_t o) {
       return rope ? (o * (uint32_t)(NT * p.M)) / C * (kTileRows / 4) : (o * total4) / C;
@@ -659,6 +659,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (et == 0 && !(p.flags & FQKV_FLAG_TEST_WITHHOLD)) mbar_arrive(normed_bar);
     if (et == 0) FQKV_TRACE_POINT(10);
 
+    // Rotary split: unit u of this CTA's share is 8 features (rows r8 .. r8 + 7 of local
+    // block lb) of one token; a thread's first unit's cos / sin are loaded before the MMAs
+    // finish, so that their latency stays out of the tail.
+    struct RopeUnit {
+      uint32_t lb;
+      int r8, m, nn, head, j;
+      int64_t b, sq;
+    };
+    auto rope_unit = [&](uint32_t u) {
+      RopeUnit r;
+      r.lb = u / (kTileRows / 8);
+      r.r8 = (int)(u - r.lb * (kTileRows / 8)) * 8;
+      const uint32_t mn = share(rank) / (kTileRows / 4) + r.lb;
+      const int nt = (int)(mn % NT);
+      r.m = (int)(mn / NT);
+      r.nn = n_base + nt * kTileRows + r.r8;
+      r.head = p.head_dim == 128 ? r.nn >> 7 : r.nn >> 6;  // head_dim is 64 or 128 on this path
+      r.j = r.nn - r.head * p.head_dim;  // the 8 features stay in one half of a head
+      r.b = (int64_t)((uint32_t)r.m / (uint32_t)p.S);  // M <= 32 tokens
+      r.sq = r.m - r.b * p.S;
+      return r;
+    };
+    const uint32_t rope_units = rope ? (share(rank + 1) - share(rank)) / (kTileRows / 4) * (kTileRows / 8) : 0u;
+    uint4 cos0 = make_uint4(0, 0, 0, 0), sin0 = make_uint4(0, 0, 0, 0);
+    if (!GRID && rope && (uint32_t)et < rope_units) {
+      const RopeUnit r = rope_unit((uint32_t)et);
+      if (r.nn < p.N && r.head < p.n_q + p.n_kv) {
+        const int64_t cs = r.b * p.cs_batch_stride + r.sq * p.head_dim + r.j;
+        cos0 = __ldg(reinterpret_cast<const uint4*>(p.cos + cs));
+        sin0 = __ldg(reinterpret_cast<const uint4*>(p.sin + cs));
+      }
+    }
     ok = mbar_wait(accum_bar, 0) && ok;
     if (et == 0) FQKV_TRACE_POINT(13);
     tc_fence_after();
@@ -815,26 +847,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         asm volatile("bar.sync 1, 256;" ::: "memory");
         const int d = p.head_dim, hd = d / 2;
-        const uint32_t b0 = f0 / (kTileRows / 4), nblk = (f1 - f0) / (kTileRows / 4);
-        for (uint32_t u = et; u < nblk * (kTileRows / 8); u += kNormThreads) {
-          const uint32_t lb = u / (kTileRows / 8);
-          const int r8 = (int)(u - lb * (kTileRows / 8)) * 8;
-          const uint32_t mn = b0 + lb;
-          const int nt = (int)(mn % NT), m = (int)(mn / NT);
-          const int nn = n_base + nt * kTileRows + r8;
+        for (uint32_t u = et; u < rope_units; u += kNormThreads) {
+          const RopeUnit ru = rope_unit(u);
+          const int r8 = ru.r8, nn = ru.nn, head = ru.head, j = ru.j;
+          const int64_t b = ru.b, sq = ru.sq;
           if (nn >= p.N) continue;
-          const int head = nn / d, j = nn - head * d;  // the 8 features stay in one half of a head
-          const int64_t b = m / p.S, sq = m - b * p.S;
-          const uint16_t* blk = tout + lb * kTileRows;
+          const uint16_t* blk = tout + ru.lb * kTileRows;
           uint16_t xv[8], ov[8];
           *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(blk + r8);
           uint16_t* dst;
           if (head < p.n_q + p.n_kv) {
             uint16_t yv[8], cv[8], sv[8];
             *reinterpret_cast<uint4*>(yv) = *reinterpret_cast<const uint4*>(blk + (r8 ^ hd));  // other half
-            const int64_t cs = b * p.cs_batch_stride + sq * d + j;
-            *reinterpret_cast<uint4*>(cv) = __ldg(reinterpret_cast<const uint4*>(p.cos + cs));
-            *reinterpret_cast<uint4*>(sv) = __ldg(reinterpret_cast<const uint4*>(p.sin + cs));
+            if (u == (uint32_t)et) {  // loaded before the MMAs finished
+              *reinterpret_cast<uint4*>(cv) = cos0;
+              *reinterpret_cast<uint4*>(sv) = sin0;
+            } else {
+              const int64_t cs = b * p.cs_batch_stride + sq * d + j;
+              *reinterpret_cast<uint4*>(cv) = __ldg(reinterpret_cast<const uint4*>(p.cos + cs));
+              *reinterpret_cast<uint4*>(sv) = __ldg(reinterpret_cast<const uint4*>(p.sin + cs));
+            }
             const bool first = j < hd;
 #pragma unroll
             for (int e = 0; e < 8; ++e)  // first half: x * cos + (-y) * sin; second: x * cos + y * sin
