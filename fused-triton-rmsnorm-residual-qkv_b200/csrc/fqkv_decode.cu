@@ -49,6 +49,8 @@ constexpr int kNormWarps = 8;                  // warps 2 .. 9: norm, then epilo
 constexpr int kNormThreads = kNormWarps * 32;
 constexpr int kThreads = 64 + kNormThreads;
 static_assert(kThreads == kDecodeThreads, "fqkv_kernels.cuh states the decode kernel's block size");
+// Portable cluster sizes only: 16-CTA clusters (non-portable) were measured slower on the
+// small per-GPU weight slices that could use them (N = 768: 7.70 against 7.37 us at C = 8).
 constexpr int kMaxCluster = 8;
 constexpr int kTileRows = 128;      // rows of W per MMA (UMMA M)
 constexpr int kKBlock = 64;         // K elements per stage (128 bytes of 16-bit data)
@@ -72,29 +74,29 @@ struct Layout {
 // slots alias buffers a peer may still be using, so the cluster agrees that every CTA's MMAs
 // have retired before any copy; a region of its own takes copies at any time.
 constexpr int kRecvRing = 0, kRecvNormed = 1, kRecvOwn = kDecodeRecvOwn;
-__host__ __device__ constexpr uint32_t recv_own_bytes(int nt, int mpad) {
+__host__ __device__ constexpr uint32_t recv_own_bytes(int nt, int mpad, int cluster) {
   // C slots of at most 32 * ceil(nt * mpad / C) quads (shares of whole 128-row blocks)
-  return (uint32_t)(nt * mpad + kMaxCluster) * 128 * 4;
+  return (uint32_t)(nt * mpad + cluster) * 128 * 4;
 }
 
 // f8 (the e4m3 terms of each activation, 0 for 16-bit weights): the ring holds e4m3 tiles
 // (128-byte rows of two k-blocks, 128-byte swizzle); the activation buffer holds f8 regions
 // of mpad x 128 bytes per two k-blocks (at least the 16-bit buffer the norm's first pass
 // fills).
-__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max, int f8 = 0,
-                                              int recv_mode = kRecvRing) {
+__host__ __device__ inline Layout make_layout(int stages, int nt, int mpad, int nkb_max, int f8, int recv_mode,
+                                              int cluster) {
   Layout L;
   L.stage_bytes = nt * kWTileBytes;
   L.ring = 0;
   L.normed = L.ring + stages * L.stage_bytes;  // 1024-aligned: stages are multiples of 16 KB
   const int act_regions = f8 ? (nkb_max + 1) / 2 * f8 : nkb_max;
   L.gain = L.normed + (uint32_t)act_regions * mpad * 128;  // [nkb_max * 64] fp32 gain slice
-  L.red = L.gain + (uint32_t)nkb_max * kKBlock * 4;    // [kMaxCluster][mpad] floats
-  L.rowp = L.red + kMaxCluster * mpad * 4;            // [mpad] floats
+  L.red = L.gain + (uint32_t)nkb_max * kKBlock * 4;  // [max(C, norm warps)][mpad] floats
+  L.rowp = L.red + (uint32_t)(cluster > kNormWarps ? cluster : kNormWarps) * mpad * 4;  // [mpad] floats
   L.rstd = L.rowp + mpad * 4;                         // [mpad] floats
   L.rscale = L.rstd + mpad * 4;                       // f8: [mpad] 2^-s of each token's terms
   L.recvd = (L.rscale + mpad * 4 + 15) & ~15u;        // kRecvOwn: the C receive slots
-  L.bars = (L.recvd + (recv_mode == kRecvOwn ? recv_own_bytes(nt, mpad) : 0u) + 7) & ~7u;
+  L.bars = (L.recvd + (recv_mode == kRecvOwn ? recv_own_bytes(nt, mpad, cluster) : 0u) + 7) & ~7u;
   // bars: full[S], empty[S], accum, normed, sum, part, acts, recv
   L.tmem_slot = L.bars + (2 * stages + 6) * 8;
   L.total = L.tmem_slot + 16;
@@ -121,7 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   FQKV_TRACE_DECL
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Layout L = make_layout(stages, NT, MPAD, p.nkb_max, F8 ? f8_terms(std::is_same<T, __nv_bfloat16>::value) : 0,
-                               p.recv_in_normed);
+                               p.recv_in_normed, (int)gridDim.x);
   uint8_t* ring = smem + L.ring;
   uint8_t* normed = smem + L.normed;
   float* red = reinterpret_cast<float*>(smem + L.red);
@@ -157,7 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t C = gridDim.x;
   const uint32_t rank = GRID ? blockIdx.x : cluster_ctarank();
   static_assert(!(GRID && (F8 || MPAD != 16)), "the grid variant takes 16-bit weights and at most 16 rows");
-  static_assert(kNormWarps <= kMaxCluster, "the grid variant's per-warp row sums use the cluster sum slots");
   // Hand-offs wait by polling their mbarrier (test_wait) when p.poll, else in try_wait.
   const int KB = p.kb_total;
   const int kb0 = decode_slice_begin((int)rank, (int)C, KB, F8), kb1 = decode_slice_begin((int)rank + 1, (int)C, KB, F8);
@@ -995,7 +996,7 @@ constexpr size_t kSmemLimit = 232448;  // max dynamic shared memory per block on
 
 size_t decode_smem_bytes(const DecodeConfig& c, int kb_total) {
   const int nkb_max = decode_slice_max(c.cluster, kb_total, c.f8 != 0);
-  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8, c.recv_in_normed).total;
+  return 1024 + make_layout(c.stages, c.nt, c.mpad, nkb_max, c.f8, c.recv_in_normed, c.cluster).total;
 }
 
 // Choose (tile rows, cluster size, ring depth).  Candidates must fit shared memory and
