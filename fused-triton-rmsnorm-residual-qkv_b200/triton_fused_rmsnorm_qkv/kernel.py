@@ -387,8 +387,9 @@ def fused_add_rmsnorm_matmul_fp8w(
 
     ``out = dtype(weight_scale[n] * sum_k normed[m, k] * weight_e4m3[n, k])`` with ``normed``
     exactly as the 16-bit path forms it (``quantize_weight_e4m3`` makes the pair from a 16-bit
-    weight).  The fused decode kernel streams the one-byte weight -- half the bytes -- and
-    converts it exactly in shared memory before the tensor-core MMA.  Decode sizes only
+    weight).  The fused decode kernel streams the one-byte weight -- half the bytes -- into
+    e4m3 x e4m3 tensor-core MMAs (tcgen05 kind::f8f6f4), the normalised activations split
+    exactly into e4m3 terms with a power-of-two scale per token.  Decode sizes only
     (M = B * S <= 64); larger M raise ``ValueError``.
     """
     assert x.is_cuda, "Fused kernel requires CUDA tensors"
