@@ -3,7 +3,9 @@
 Every ``csrc/*.cu`` file is compiled with nvcc for ``sm_100a`` (in parallel) and
 linked into one position-independent shared object with the CUDA runtime linked
 statically, so the library needs only the NVIDIA driver at run time.  The library is
-built in-tree (next to the Python package that loads it).
+built in-tree (next to the Python package that loads it).  ``csrc/fqkv_pycall.c``, the
+package's CPython fast path for ``fqkv_launch``, is compiled with the host C compiler
+when the Python headers are present (the package falls back to ctypes otherwise).
 
 Usage: ``python build.py [--verbose] [--ptxas-info]``
 """
@@ -14,6 +16,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
@@ -52,6 +55,10 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
     if LIB.exists() and not force:
         newest = max(p.stat().st_mtime for p in sources + headers + [Path(__file__)])
         if LIB.stat().st_mtime >= newest:
+            pycall = sorted(OUT_DIR.glob("_fqkv_pycall*.so"))
+            src = CSRC / "fqkv_pycall.c"
+            if not pycall or (src.exists() and pycall[-1].stat().st_mtime < src.stat().st_mtime):
+                build_pycall(verbose)
             return LIB
     BUILD.mkdir(exist_ok=True)
     cc = nvcc()
@@ -70,7 +77,23 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
     tmp = LIB.with_suffix(".so.tmp")
     _run([cc, *ARCH, "-shared", "-rdc=true", "-cudart", "static", "-o", str(tmp), *[str(o) for o, _ in results]], verbose)
     os.replace(tmp, LIB)
+    build_pycall(verbose)
     return LIB
+
+
+def build_pycall(verbose: bool = False) -> Path | None:
+    """Compile the CPython fast path (``_fqkv_pycall``) next to the package, or return None
+    when the host compiler or the Python headers are missing."""
+    src = CSRC / "fqkv_pycall.c"
+    include = sysconfig.get_paths().get("include", "")
+    cc = shutil.which(os.environ.get("CC", "gcc")) or shutil.which("cc")
+    if not src.exists() or not cc or not (Path(include) / "Python.h").exists():
+        return None
+    dst = OUT_DIR / ("_fqkv_pycall" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+    tmp = dst.with_name(dst.name + ".tmp")
+    _run([cc, "-O2", "-shared", "-fPIC", "-I", include, str(src), "-o", str(tmp)], verbose)
+    os.replace(tmp, dst)
+    return dst
 
 
 def main() -> int:

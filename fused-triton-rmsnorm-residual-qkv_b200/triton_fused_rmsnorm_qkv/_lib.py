@@ -58,6 +58,11 @@ class ScheduleInfo(ctypes.Structure):
 
 
 _lib = None
+# CPython fast path for fqkv_launch (csrc/fqkv_pycall.c, built by build.py); ctypes otherwise.
+try:
+    from . import _fqkv_pycall as _pycall
+except ImportError:
+    _pycall = None
 
 
 def load() -> ctypes.CDLL:
@@ -97,6 +102,8 @@ def load() -> ctypes.CDLL:
     lib.fqkv_launch_rope.argtypes = [vp, vp, vp, i32, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp, vp,
                                      i64, i32, i32, i32, f32, i32, i32, vp]
     lib.fqkv_launch_rope.restype = i32
+    if _pycall is not None:
+        _pycall.set_launch(ctypes.cast(lib.fqkv_launch, ctypes.c_void_p).value)
     _lib = lib
     return lib
 
@@ -119,8 +126,12 @@ def check(rc: int, what: str = "fqkv_launch") -> None:
 
 def launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw, ldo, ldro, eps,
            dtype, schedule, flags, ws_ptr, ws_bytes, stream) -> int:
-    return load().fqkv_launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw,
-                              ldo, ldro, ctypes.c_float(eps), dtype, schedule, flags, ws_ptr, ws_bytes, stream)
+    lib = _lib if _lib is not None else load()
+    if _pycall is not None:  # the same library call, its arguments converted by the CPython module
+        return _pycall.launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw, ldo,
+                              ldro, eps, dtype, schedule, flags, ws_ptr, ws_bytes, stream)
+    return lib.fqkv_launch(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw,
+                           ldo, ldro, ctypes.c_float(eps), dtype, schedule, flags, ws_ptr, ws_bytes, stream)
 
 
 def launch_fp8w(x_ptr, r_ptr, g_ptr, g_dtype, w_ptr, scale_ptr, out_ptr, rout_ptr, M, H, N, ldx, ldr, ldw, ldo,

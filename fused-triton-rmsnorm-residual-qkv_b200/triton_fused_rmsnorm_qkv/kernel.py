@@ -98,6 +98,12 @@ def _schedule_code(schedule) -> int:
     return int(schedule)
 
 
+def _current_device() -> int:
+    """Index of the current CUDA device (without torch.cuda's lazy-initialisation checks)."""
+    raw = getattr(torch._C, "_cuda_getDevice", None)
+    return raw() if raw is not None else torch.cuda.current_device()
+
+
 def _current_stream(index: int) -> int:
     """Handle of the current CUDA stream of device ``index`` (without building a Stream object)."""
     raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -221,7 +227,7 @@ def _launch(x2: torch.Tensor, r2: Optional[torch.Tensor], rms_weight: torch.Tens
     ldx, ldw, ldo = _row_stride(x2), w.stride(0), _row_stride(out2)
     ldr = _row_stride(r2) if r2 is not None else 0
     ldro = _row_stride(rout2) if rout2 is not None else 0
-    if index == torch.cuda.current_device():
+    if index == _current_device():
         rc = _call(x2, r2, g, gcode, w, out2, rout2, M, H, N, ldx, ldr, ldw, ldo, ldro, eps, dt, code, flags, index)
     else:
         with torch.cuda.device(index):
@@ -254,7 +260,7 @@ def _call(x2, r2, g, gcode, w, out2, rout2, M, H, N, ldx, ldr, ldw, ldo, ldro, e
         float(eps), dt, code, flags, ws.data_ptr() if ws is not None else None, ws_bytes, stream)
 
 
-def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, static_weights):
+def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, static_weights, out=None):
     assert x.is_cuda, "Fused kernel requires CUDA tensors"
     B, S, H = x.shape
     N_OUT = weight.shape[0]
@@ -266,10 +272,15 @@ def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, stat
         if residual.numel() != M * H:
             raise ValueError(f"residual must match x {tuple(x.shape)}, got {tuple(residual.shape)}")
         r2 = _rows(residual, M, H)
-    out = torch.empty(B, S, N_OUT, dtype=x.dtype, device=x.device)
+    if out is None:
+        out = torch.empty(B, S, N_OUT, dtype=x.dtype, device=x.device)
+    elif (out.shape != (B, S, N_OUT) or out.dtype != x.dtype or out.get_device() != x.get_device()
+          or out.stride(2) != 1 or (B > 1 and out.stride(0) != S * out.stride(1))):
+        raise ValueError(f"out must be a ({B}, {S}, {N_OUT}) {x.dtype} tensor on {x.device} whose rows are "
+                         "uniformly strided with unit stride along N")
     rout2 = None
     if residual_out is not None:
-        if residual_out.numel() != M * H or residual_out.dtype != x.dtype or residual_out.device != x.device:
+        if residual_out.numel() != M * H or residual_out.dtype != x.dtype or residual_out.get_device() != x.get_device():
             raise ValueError("residual_out must have the shape, dtype and device of x")
         rout2 = _rows(residual_out, M, H)
         if rout2.data_ptr() != residual_out.data_ptr() or rout2.stride(-1) != 1:
@@ -290,6 +301,7 @@ def fused_rmsnorm_residual_matmul(
     residual_out: Optional[torch.Tensor] = None,
     schedule=None,
     static_weights: Optional[bool] = None,
+    out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Fused (optional residual) + RMSNorm + arbitrary-width matmul (kernel.py:363-436).
 
@@ -303,12 +315,14 @@ def fused_rmsnorm_residual_matmul(
         schedule: None/"auto", "decode", "grid", "split", "prefill" or "simt" ("naive").
         static_weights: weight is not written by the preceding kernel in the stream
             (default: environment variable FQKV_STATIC_WEIGHTS).
+        out: optional (B, S, N_OUT) tensor in x.dtype that receives the result (rows
+            uniformly strided, unit stride along N) instead of a new allocation.
 
     Returns:
-        (B, S, N_OUT) tensor in x.dtype.
+        (B, S, N_OUT) tensor in x.dtype (``out`` when given).
     """
     return _fused(x, residual, rms_weight, weight, eps, residual_out=residual_out, schedule=schedule,
-                  static_weights=static_weights)
+                  static_weights=static_weights, out=out)
 
 
 def fused_add_rmsnorm_matmul(
@@ -321,16 +335,21 @@ def fused_add_rmsnorm_matmul(
     return_residual: bool = True,
     schedule=None,
     static_weights: Optional[bool] = None,
+    out: Optional[torch.Tensor] = None,
+    residual_out: Optional[torch.Tensor] = None,
 ):
     """As ``fused_rmsnorm_residual_matmul``, also returning the updated residual.
 
     Returns ``(out, hidden)`` with ``hidden = x + residual`` computed once in fp32 and
     rounded to x.dtype (bit-identical to ``x + residual`` in PyTorch, baseline.py:48),
-    or ``out`` alone when ``return_residual`` is False.
+    or ``out`` alone when ``return_residual`` is False.  ``out`` and ``residual_out``
+    (with ``return_residual``) receive the two results instead of new allocations.
     """
-    hidden = torch.empty_like(x) if return_residual else None
+    hidden = None
+    if return_residual:
+        hidden = residual_out if residual_out is not None else torch.empty_like(x)
     out = _fused(x, residual, rms_weight, weight, eps, residual_out=hidden, schedule=schedule,
-                 static_weights=static_weights)
+                 static_weights=static_weights, out=out)
     return (out, hidden) if return_residual else out
 
 
