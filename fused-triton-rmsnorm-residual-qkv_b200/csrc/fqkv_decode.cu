@@ -159,7 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t C = gridDim.x;
   const uint32_t rank = GRID ? blockIdx.x : cluster_ctarank();
   static_assert(!(GRID && (F8 || MPAD != 16)), "the grid variant takes 16-bit weights and at most 16 rows");
-  // Hand-offs wait by polling their mbarrier (test_wait) when p.poll, else in try_wait.
   const int KB = p.kb_total;
   const int kb0 = decode_slice_begin((int)rank, (int)C, KB, F8), kb1 = decode_slice_begin((int)rank + 1, (int)C, KB, F8);
   const int nkb = kb1 - kb0;
@@ -169,6 +168,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Accumulators [0, NT * kTerms * MPAD): tile nt's term t in columns (nt * kTerms + t) * MPAD.
   constexpr uint32_t kTmemCols = tmem_cols_for(NT * kTerms * MPAD);
   constexpr int kBoxTiles = decode_box_tiles(NT);
+
+  // The tile's partial sums are reduced in 16-byte quads (4 output features): quad
+  // f = ((m * NT + nt) * 128 + row) / 4 for token m < M; rank o reduces [F(o), F(o+1)).
+  // With the rotary split, shares are whole 128-row blocks (m, nt): a head's two halves stay
+  // with one CTA.
+  const bool rope = !F8 && !GRID && p.q != nullptr;  // the rotary split: 16-bit weights, cluster kernel
+  const uint32_t total4 = (uint32_t)(NT * p.M * (kTileRows / 4));
+  auto share = [&](uint32_t o) {
+    return rope ? (o * (uint32_t)(NT * p.M)) / C * (kTileRows / 4) : (o * total4) / C;
+  };
+  const uint32_t slot_bytes = rope ? 16u * (kTileRows / 4) * ((NT * MPAD + C - 1) / C)
+                                   : 16u * ((NT * MPAD * (kTileRows / 4) + C - 1) / C);
 
   // ---------------------------------------------------------------- setup
   FQKV_TRACE_BEGIN();
@@ -184,6 +195,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acts_bar, 1);
     mbar_init(recv_bar, 1);     // local arrive + the peers' bulk copies (complete_tx)
     fence_mbarrier_init_cluster();
+    // This CTA expects C * MPAD row sums (4 bytes each) from the cluster's st.async writes,
+    // and later C - 1 bulk copies of its share of the tile; both are declared before the
+    // CTA's first cluster arrival, so no peer's write can come first.
+    if (!GRID) {
+      mbar_arrive_expect_tx_cluster(sum_bar, C * MPAD * 4);
+      mbar_arrive_expect_tx_cluster(recv_bar, (C - 1) * 16u * (share(rank + 1) - share(rank)));
+    }
   }
   const int nstage = F8 ? (nkb + 1) / 2 : nkb;  // e4m3: a ring stage holds two k-blocks
   auto issue_stage = [&](int i, int s, uint64_t pol_w) {
@@ -200,9 +218,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
+  // The CTA's barriers and TMEM address are visible to its own threads after this barrier;
+  // its cluster arrival publishes the barriers to the peers, and a thread waits for the
+  // whole cluster only before its first access to a peer (the norm warps before the row-sum
+  // exchange; the other warps before leaving), so that the weight stream and the activation
+  // loads do not wait for the cluster's slowest CTA to be set up.
   tc_fence_before();
-  cluster_sync();  // every CTA of the cluster is running and has initialised its barriers
+  __syncthreads();
   tc_fence_after();
+  cluster_arrive_release();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (threadIdx.x == 0) FQKV_TRACE_POINT(3);
@@ -308,23 +332,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j < nchunk && k < p.H) load_gain8_raw(p.g, p.gdt, k, graw[i]);
       }
     };
-    // The tile's partial sums are reduced in 16-byte quads (4 output features): quad
-    // f = ((m * NT + nt) * 128 + row) / 4 for token m < M; rank o reduces [F(o), F(o+1)).
-    // With the rotary split, shares are whole 128-row blocks (m, nt): a head's two halves stay
-    // with one CTA.
-    const bool rope = !F8 && !GRID && p.q != nullptr;  // the rotary split: 16-bit weights, cluster kernel
-    const uint32_t total4 = (uint32_t)(NT * p.M * (kTileRows / 4));
-    auto share = [&](uint32_t o) {
-      return rope ? (o * (uint32_t)(NT * p.M)) / C * (kTileRows / 4) : (o * total4) / C;
-    };
-    const uint32_t slot_bytes = rope ? 16u * (kTileRows / 4) * ((NT * MPAD + C - 1) / C)
-                                     : 16u * ((NT * MPAD * (kTileRows / 4) + C - 1) / C);
-    // This CTA expects C * MPAD row sums (4 bytes each) from the cluster's st.async writes,
-    // and later C - 1 bulk copies of its share of the tile.
-    if (!GRID && et == 0) {
-      mbar_arrive_expect_tx_cluster(sum_bar, C * MPAD * 4);
-      mbar_arrive_expect_tx_cluster(recv_bar, (C - 1) * 16u * (share(rank + 1) - share(rank)));
-    }
     if (static_w) issue_gain();
     // Warm L2 with this CTA's slice of x and the residual (one prefetch per 128-byte line)
     // while the preceding grid may still be running: a prefetch moves no data into
@@ -479,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every activation load has returned: the producer may now fill the whole ring.
     if (et == 0) mbar_arrive(acts_bar);
     if (et == 0) FQKV_TRACE_POINT(8);
+    cluster_wait_acquire();  // every CTA of the cluster has initialised its barriers
     if constexpr (GRID) {
       // Whole-row sums: the eight warps' shares, added in warp order.
       for (int m = et; m < p.M; m += kNormThreads) {
@@ -890,6 +898,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------------------------------------------------------- teardown
   if (warp < 2) {
     __syncwarp();
+    cluster_wait_acquire_thread();  // the set-up phase of the cluster barrier
     tc_fence_before();
     cluster_arrive_relaxed_thread();
   }
