@@ -60,3 +60,31 @@ def test_fp8w_rejects_prefill_sizes():
     with pytest.raises(ValueError):
         fused_add_rmsnorm_matmul_fp8w(x, None, torch.ones(256, device="cuda"), w8,
                                       torch.ones(512, device="cuda"), 1e-5)
+
+
+@pytest.mark.parametrize("M", [1, 32, 64])
+def test_llama3_8b_decode_fp8w_fp16_sizes(M):
+    """fp16 activations take three e4m3 terms; above 32 rows they run as two launches."""
+    run_fp8(M, 4096, 6144, torch.float16, seed=70 + M)
+
+
+@pytest.mark.parametrize("dtype,min_equal", [(torch.bfloat16, 0.99), (torch.float16, 0.97)])
+def test_fp8w_term_split_is_exact(dtype, min_equal):
+    """The activations' e4m3 terms hold the normalised values exactly, so the kernel differs
+    from the fp64 oracle only by its fp32 accumulation: nearly every output is bit-identical,
+    and none is further away than one unit in the last place plus the fp32 rounding of a
+    4096-term sum (1e-5 of the largest output; it dominates only for outputs near zero)."""
+    M, H, N = 16, 4096, 6144
+    x, r, g, w = make_case(M, H, N, dtype, seed=91)
+    w8, scale = quantize_weight_e4m3(w)
+    out, _ = fused_add_rmsnorm_matmul_fp8w(x.cuda()[None], r.cuda()[None], g.cuda(), w8.cuda(), scale.cuda(), 1e-5)
+    torch.cuda.synchronize()
+    ref, _ = forward_fp8w(x, r, g, w8, scale, 1e-5)
+    got = out[0].cpu()
+    equal = (got == ref).float().mean().item()
+    assert equal >= min_equal, equal
+    # one unit in the last place of the dtype at each reference value (away from zero)
+    away = torch.where(ref >= 0, torch.tensor(float("inf"), dtype=dtype), torch.tensor(float("-inf"), dtype=dtype))
+    step = (torch.nextafter(ref, away).float() - ref.float()).abs()
+    tol = step + 1e-5 * ref.float().abs().max()
+    assert bool(((got.float() - ref.float()).abs() <= tol).all())
