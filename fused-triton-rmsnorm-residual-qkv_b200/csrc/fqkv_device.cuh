@@ -184,33 +184,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred P;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, P;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// As mbar_wait (CTA scope), polling with the non-blocking test_wait: for hand-offs between
-// threads of the CTA that come in quick succession, where a suspended try_wait would add
-// its wake-up delay to every step.  Bounded the same way.
-__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns(), limit = *(volatile unsigned long long*)&g_wait_limit_ns;
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u && globaltimer_ns() - t0 > limit) {
-      record_status(FQKV_STATUS_WAIT_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 // AND of `v` over the `count` threads meeting at named barrier `id` (uniform result).
 __device__ __forceinline__ bool bar_and(int id, int count, bool v) {
   uint32_t r;
