@@ -474,6 +474,31 @@ def eager_flushed_us(fn_step, n: int, dev) -> float:
     return statistics.median(times)
 
 
+def after_other_kernel_us(fn_step, steps: int, dev) -> float:
+    """Microseconds one step adds to a CUDA graph when it follows an ordinary PyTorch kernel
+    (an elementwise op on a 4 KB tensor, launched without programmatic dependent launch), as in
+    a model whose preceding op is not this library's: graph of [other, step] x K minus graph of
+    [other] x K.  Nothing of the step overlaps a preceding step; the launch itself is pipelined
+    by the graph, as in a graph-captured model."""
+    other = torch.zeros(1024, device=dev)
+
+    def pair(i):
+        other.mul_(1.0)
+        fn_step(i)
+
+    t_pair = time_graph(pair, steps, 5, dev, replays=20) / steps
+    t_other = time_graph(lambda i: other.mul_(1.0), steps, 5, dev, replays=20) / steps
+    return (t_pair - t_other) * 1e3
+
+
+def eager_event_floor_us(dev, n: int = 50) -> float:
+    """What the eager, event-bracketed measurement of eager_flushed_us reports for a kernel that
+    does almost nothing (the same 4 KB elementwise op), after the same 256 MB memset: the launch
+    and event overhead contained in every eager_flushed_us figure."""
+    other = torch.zeros(1024, device=dev)
+    return eager_flushed_us(lambda i: other.mul_(1.0), n, dev)
+
+
 def run_detail(wl_default: dict, dev, peaks: dict, args_triton_comparator: str = "autotune") -> dict:
     from triton_fused_rmsnorm_qkv import _lib
     from triton_fused_rmsnorm_qkv.kernel import schedule_info
@@ -500,6 +525,9 @@ def run_detail(wl_default: dict, dev, peaks: dict, args_triton_comparator: str =
             entry["speedup_vs_torch_unfused"] = round(t_ref / t_ms, 2)
             if mm <= 64:
                 entry["eager_l2_flushed_us"] = round(eager_flushed_us(op_step_fn(ss, wl["eps"], mm), 50, dev), 3)
+                entry["eager_event_floor_us"] = round(eager_event_floor_us(dev), 3)
+                entry["graph_after_other_kernel_us"] = round(after_other_kernel_us(op_step_fn(ss, wl["eps"], mm),
+                                                                                   200, dev), 3)
         detail[label] = entry
         del ss
     detail.update(run_fp8w_detail(dev, peaks))

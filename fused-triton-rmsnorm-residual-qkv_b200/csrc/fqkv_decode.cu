@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx_cluster(sum_bar, C * MPAD * 4);
       mbar_arrive_expect_tx_cluster(recv_bar, (C - 1) * 16u * (share(rank + 1) - share(rank)));
     }
+    FQKV_TRACE_POINT(17);
   }
   const int nstage = F8 ? (nkb + 1) / 2 : nkb;  // e4m3: a ring stage holds two k-blocks
   auto issue_stage = [&](int i, int s, uint64_t pol_w) {
@@ -214,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        n_base + j * kTileRows, pol_w);
   };
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tmW);
+  if (threadIdx.x == 0) FQKV_TRACE_POINT(18);
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -225,6 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // loads do not wait for the cluster's slowest CTA to be set up.
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) FQKV_TRACE_POINT(21);
   tc_fence_after();
   cluster_arrive_release();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
@@ -909,7 +912,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
-  if (threadIdx.x == 0) FQKV_TRACE_END();
+  FQKV_TRACE_END();
 }
 
 template <int MPAD, int NT, bool F8, bool GRID = false>

@@ -47,7 +47,12 @@ __device__ __forceinline__ unsigned long long clock64_now() {
   asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
   return t;
 }
-#define FQKV_TRACE_DECL __shared__ unsigned int fqkv_trace_idx_;
+// The stamps are kept in shared memory while the kernel runs and written out by
+// FQKV_TRACE_END; the record index (a global atomic) is requested at entry but first used at
+// the end, so its latency stays off the traced path.
+#define FQKV_TRACE_DECL                                                                                  \
+  __shared__ unsigned long long fqkv_trace_s_[::fqkv::kTraceSlots];                                      \
+  unsigned int fqkv_trace_i_ = 0xFFFFFFFFu;
 // Thread 0, before the kernel's first block-wide barrier.
 #define FQKV_TRACE_BEGIN()                                                                               \
   do {                                                                                                   \
@@ -57,34 +62,28 @@ __device__ __forceinline__ unsigned long long clock64_now() {
       const unsigned long long c0 = ::fqkv::clock64_now();                                               \
       unsigned int smid;                                                                                 \
       asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));                                                  \
-      const unsigned int i = ::fqkv::g_trace_buf ? atomicAdd(&::fqkv::g_trace_ctr, 1u) : 0xFFFFFFFFu;   \
-      fqkv_trace_idx_ = i < ::fqkv::g_trace_cap ? i : 0xFFFFFFFFu;                                      \
-      if (fqkv_trace_idx_ != 0xFFFFFFFFu) {                                                              \
-        unsigned long long* r = ::fqkv::g_trace_buf + (size_t)fqkv_trace_idx_ * ::fqkv::kTraceSlots;     \
-        r[0] = (unsigned long long)blockIdx.x | ((unsigned long long)blockIdx.y << 16) |                 \
-               ((unsigned long long)smid << 32) | ((unsigned long long)gridDim.x << 40) |                \
-               ((unsigned long long)gridDim.y << 48);                                                    \
-        r[1] = g0;                                                                                       \
-        r[2] = c0;                                                                                       \
-      }                                                                                                  \
+      if (::fqkv::g_trace_buf) fqkv_trace_i_ = atomicAdd(&::fqkv::g_trace_ctr, 1u);                      \
+      for (int s_ = 3; s_ < ::fqkv::kTraceSlots; ++s_) fqkv_trace_s_[s_] = 0ull;                         \
+      fqkv_trace_s_[0] = (unsigned long long)blockIdx.x | ((unsigned long long)blockIdx.y << 16) |       \
+                         ((unsigned long long)smid << 32) | ((unsigned long long)gridDim.x << 40) |      \
+                         ((unsigned long long)gridDim.y << 48);                                          \
+      fqkv_trace_s_[1] = g0;                                                                             \
+      fqkv_trace_s_[2] = c0;                                                                             \
     }                                                                                                    \
   } while (0)
-// Only after the barrier that follows FQKV_TRACE_BEGIN (the record index is in shared memory);
-// the index is checked against the buffer's capacity before any write.
-#define FQKV_TRACE_POINT(slot)                                                                           \
-  do {                                                                                                   \
-    const unsigned int fqkv_ti_ = fqkv_trace_idx_;                                                       \
-    if (fqkv_ti_ < ::fqkv::g_trace_cap && ::fqkv::g_trace_buf)                                           \
-      ::fqkv::g_trace_buf[(size_t)fqkv_ti_ * ::fqkv::kTraceSlots + (slot)] = ::fqkv::clock64_now();      \
-  } while (0)
+// Only after the barrier that follows FQKV_TRACE_BEGIN.
+#define FQKV_TRACE_POINT(slot) (fqkv_trace_s_[(slot)] = ::fqkv::clock64_now())
+// Every thread of the block, once all of them have made their last stamp.
 #define FQKV_TRACE_END()                                                                                 \
   do {                                                                                                   \
-    if (fqkv_trace_idx_ < ::fqkv::g_trace_cap && ::fqkv::g_trace_buf) {                                  \
+    __syncthreads();                                                                                     \
+    if (threadIdx.x == 0 && fqkv_trace_i_ < ::fqkv::g_trace_cap) {                                       \
       unsigned long long g1;                                                                             \
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));                                             \
-      unsigned long long* r = ::fqkv::g_trace_buf + (size_t)fqkv_trace_idx_ * ::fqkv::kTraceSlots;       \
-      r[::fqkv::kTraceSlots - 2] = ::fqkv::clock64_now();                                                        \
-      r[::fqkv::kTraceSlots - 1] = g1;                                                                           \
+      fqkv_trace_s_[::fqkv::kTraceSlots - 2] = ::fqkv::clock64_now();                                    \
+      fqkv_trace_s_[::fqkv::kTraceSlots - 1] = g1;                                                       \
+      for (int s_ = 0; s_ < ::fqkv::kTraceSlots; ++s_)                                                   \
+        ::fqkv::g_trace_buf[(size_t)fqkv_trace_i_ * ::fqkv::kTraceSlots + s_] = fqkv_trace_s_[s_];       \
     }                                                                                                    \
   } while (0)
 #else
