@@ -48,6 +48,9 @@ namespace {
 constexpr int kNormWarps = 8;                  // warps 2 .. 9: norm, then epilogue
 constexpr int kNormThreads = kNormWarps * 32;
 constexpr int kThreads = 64 + kNormThreads;
+// Named barriers (barrier 0 is __syncthreads; 1 is the norm warps' own, 256 threads).
+constexpr int kSetupBar = 2;      // set-up of warps 0 and 1 -> the norm warps
+constexpr int kSetupPairBar = 3;  // thread 0's mbarrier initialisation -> the MMA warp
 static_assert(kThreads == kDecodeThreads, "fqkv_kernels.cuh states the decode kernel's block size");
 // Portable cluster sizes only: 16-CTA clusters (non-portable) were measured slower on the
 // small per-GPU weight slices that could use them (N = 768: 7.70 against 7.37 us at C = 8).
@@ -214,25 +217,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_2d_hint(ring + s * L.stage_bytes + j * kWTileBytes, &tmW, &full[s], (kb0 + (F8 ? 2 * i : i)) * kKBlock,
                        n_base + j * kTileRows, pol_w);
   };
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmW);
-  if (threadIdx.x == 0) FQKV_TRACE_POINT(18);
-  if (warp == 1) {
+  // Set-up without a block-wide barrier, so that no role waits for a set-up step it does not
+  // need.  Named barrier kSetupPairBar: warp 0 (thread 0 initialised the mbarriers) arrives,
+  // the MMA warp waits for it.  Named barrier kSetupBar: warps 0 and 1 arrive once the
+  // mbarriers are initialised and TMEM is allocated; the norm warps wait for it only before
+  // their first use of either (after their activation loads, which therefore start as soon as
+  // the preceding grid has been released, even in a CTA that starts late).  The cluster
+  // arrival publishes the barriers to the peers, and a thread waits for the whole cluster
+  // only before its first access to a peer (the norm warps before the row-sum exchange; the
+  // other warps before leaving), so that the weight stream and the activation loads do not
+  // wait for the cluster's slowest CTA to be set up.
+  uint32_t tmem_base = 0;
+  if (warp == 0) {
+    if (lane == 0) tma_prefetch_desc(&tmW);
+    if (lane == 0) FQKV_TRACE_POINT(18);
+    __syncwarp();
+    named_bar_arrive(kSetupPairBar, 64);
+    named_bar_arrive(kSetupBar, kThreads);
+    cluster_arrive_release();
+    if (lane == 0) pdl_launch_dependents();
+    if (lane == 0) FQKV_TRACE_POINT(3);
+  } else if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
+    tc_fence_before();
+    named_bar_sync(kSetupPairBar, 64);
+    named_bar_arrive(kSetupBar, kThreads);
+    tc_fence_after();
+    cluster_arrive_release();
+    tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+    if (lane == 0) FQKV_TRACE_POINT(21);
+  } else {
+    cluster_arrive_release();
   }
-  // The CTA's barriers and TMEM address are visible to its own threads after this barrier;
-  // its cluster arrival publishes the barriers to the peers, and a thread waits for the
-  // whole cluster only before its first access to a peer (the norm warps before the row-sum
-  // exchange; the other warps before leaving), so that the weight stream and the activation
-  // loads do not wait for the cluster's slowest CTA to be set up.
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0) FQKV_TRACE_POINT(21);
-  tc_fence_after();
-  cluster_arrive_release();
-  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
-  if (threadIdx.x == 0) pdl_launch_dependents();
-  if (threadIdx.x == 0) FQKV_TRACE_POINT(3);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -485,7 +502,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         gain_hi[j] = gv[1];
       }
     }
-    asm volatile("bar.sync 1, 256;" ::: "memory");
+    // All norm warps, and the set-up of warps 0 and 1 (mbarriers initialised, TMEM allocated).
+    named_bar_sync(kSetupBar, kThreads);
+    tc_fence_after();
+    tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
     // Every activation load has returned: the producer may now fill the whole ring.
     if (et == 0) mbar_arrive(acts_bar);
     if (et == 0) FQKV_TRACE_POINT(8);

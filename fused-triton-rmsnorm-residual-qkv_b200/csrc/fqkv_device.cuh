@@ -53,7 +53,7 @@ __device__ __forceinline__ unsigned long long clock64_now() {
 #define FQKV_TRACE_DECL                                                                                  \
   __shared__ unsigned long long fqkv_trace_s_[::fqkv::kTraceSlots];                                      \
   unsigned int fqkv_trace_i_ = 0xFFFFFFFFu;
-// Thread 0, before the kernel's first block-wide barrier.
+// Thread 0, first thing in the kernel.
 #define FQKV_TRACE_BEGIN()                                                                               \
   do {                                                                                                   \
     if (threadIdx.x == 0) {                                                                              \
@@ -63,7 +63,6 @@ __device__ __forceinline__ unsigned long long clock64_now() {
       unsigned int smid;                                                                                 \
       asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));                                                  \
       if (::fqkv::g_trace_buf) fqkv_trace_i_ = atomicAdd(&::fqkv::g_trace_ctr, 1u);                      \
-      for (int s_ = 3; s_ < ::fqkv::kTraceSlots; ++s_) fqkv_trace_s_[s_] = 0ull;                         \
       fqkv_trace_s_[0] = (unsigned long long)blockIdx.x | ((unsigned long long)blockIdx.y << 16) |       \
                          ((unsigned long long)smid << 32) | ((unsigned long long)gridDim.x << 40) |      \
                          ((unsigned long long)gridDim.y << 48);                                          \
@@ -71,7 +70,8 @@ __device__ __forceinline__ unsigned long long clock64_now() {
       fqkv_trace_s_[2] = c0;                                                                             \
     }                                                                                                    \
   } while (0)
-// Only after the barrier that follows FQKV_TRACE_BEGIN.
+// Slots a CTA does not stamp hold whatever shared memory held; readers keep only stamps
+// between the entry and exit clocks.
 #define FQKV_TRACE_POINT(slot) (fqkv_trace_s_[(slot)] = ::fqkv::clock64_now())
 // Every thread of the block, once all of them have made their last stamp.
 #define FQKV_TRACE_END()                                                                                 \
@@ -286,6 +286,14 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
+}
+
+// Named CTA barriers: `count` threads (a multiple of 32) in all; arriving threads do not wait.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void cluster_arrive_release() {
