@@ -13,10 +13,8 @@ residual add with the updated residual returned).  32 distinct seeded weight set
   value      whole-job HBM GB/s: algorithmic bytes of all ranks' steps / device time
              (max over ranks) of exactly K steps captured in one CUDA graph;
   e2e        the same metric through the public Python API with pinned host buffers:
-             every step copies x and residual host->device and runs the op with its
-             output and updated residual written straight into pinned host memory,
-             synchronising each step (`device_outputs`: results written to the device
-             and copied back by a device->host copy);
+             every step copies x and residual host->device, runs the op and copies the
+             output and updated residual device->host, synchronising each step;
   roofline   achieved GB/s of the dominant kernel vs the measured HBM copy peak;
   cpu_baseline  the CPU oracle (a restatement of the reference's baseline.py) on a
              bounded sample of the same workload, rank 0 only at N=1;
@@ -786,85 +784,66 @@ def run_sharded_detail(pg, barrier, dev, rank: int, world: int, peaks: dict) -> 
 
 def run_e2e(sets, wl: dict, M: int, H: int, N_loc: int, dtype, dev, args, pg) -> dict:
     """The metric through the public API on every rank: each step copies that step's x and
-    residual from pinned host memory to the device, runs the op on the rank's shard with its
-    output and updated residual written straight into pinned host memory (``out=`` /
-    ``residual_out=`` pinned host tensors), and synchronises.  Time per step is the max over
-    ranks of the CUDA-event (or, if longer, wall-clock) time.  ``device_outputs`` in the result:
-    the same step with the results written to device memory and copied back by a separate
-    device-to-host copy."""
+    residual from pinned host memory to the device, runs the op on the rank's shard and
+    copies its output and updated residual back, synchronising every step.  Time per step
+    is the max over ranks of the CUDA-event (or, if longer, wall-clock) time."""
     from triton_fused_rmsnorm_qkv import fused_add_rmsnorm_matmul
 
     x0, r0, g0, w0 = sets[0]
     # A step's inputs (x, then the residual) sit in one pinned host buffer and go over in
-    # one copy; its results (the output, then the updated residual) land in one pinned host
-    # buffer.  Each DMA copy costs several microseconds of latency whatever its size.
+    # one copy; its results (the output, then the updated residual) are written by the call
+    # into one device buffer (out= / residual_out=) and come back in one copy.  Each DMA
+    # copy costs several microseconds of latency whatever its size.
     n_in = 2 if r0 is not None else 1
     in_h = torch.empty(n_in, M, H, dtype=dtype).pin_memory()
     in_h[0].copy_(x0[0].cpu())
     if r0 is not None:
         in_h[1].copy_(r0[0].cpu())
     res_h = torch.empty(M * N_loc + M * H, dtype=dtype).pin_memory()
-    out_h, hid_h = res_h[:M * N_loc].view(1, M, N_loc), res_h[M * N_loc:].view(1, M, H)
     in_d = torch.empty(n_in, M, H, dtype=dtype, device=dev)
     res_d = torch.empty(M * N_loc + M * H, dtype=dtype, device=dev)
     xd = in_d[0:1]
     rd = in_d[1:2] if r0 is not None else None
     out_d, hid_d = res_d[:M * N_loc].view(1, M, N_loc), res_d[M * N_loc:].view(1, M, H)
     e2e_steps = max(10, min(args.steps, 2000))
-    stream = torch.cuda.current_stream(dev)
-    host_out = M <= 64  # the decode schedules write host memory with plain stores
 
-    def step_host_out(i):
-        _, _, g_i, w_i = sets[i % len(sets)]
-        in_d.copy_(in_h, non_blocking=True)
-        fused_add_rmsnorm_matmul(xd, rd, g_i, w_i, wl["eps"], static_weights=True, out=out_h, residual_out=hid_h)
-        stream.synchronize()
-
-    def step_copy_out(i):
+    def e2e_step(i):
         _, _, g_i, w_i = sets[i % len(sets)]
         in_d.copy_(in_h, non_blocking=True)
         fused_add_rmsnorm_matmul(xd, rd, g_i, w_i, wl["eps"], static_weights=True, out=out_d, residual_out=hid_d)
         res_h.copy_(res_d, non_blocking=True)
-        stream.synchronize()
+        torch.cuda.current_stream(dev).synchronize()
 
-    def timed(step) -> float:
-        for i in range(max(3, args.warmup)):
-            step(i)
-        if pg is not None:
-            pg.barrier()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize(dev)
-        ev0.record()
-        w0t = time.perf_counter()
-        for i in range(e2e_steps):
-            step(i)
-        ev1.record()
-        torch.cuda.synchronize(dev)
-        wall = time.perf_counter() - w0t
-        t = torch.tensor([max(ev0.elapsed_time(ev1), wall * 1e3) / e2e_steps], device=dev)
-        if pg is not None:
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
-
-    copy_ms = timed(step_copy_out)
-    e2e_ms = timed(step_host_out) if host_out else copy_ms
-    world = pg.get_world_size() if pg is not None else 1
+    for i in range(max(3, args.warmup)):
+        e2e_step(i)
+    if pg is not None:
+        pg.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    ev0.record()
+    w0t = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - w0t
+    t = torch.tensor([max(ev0.elapsed_time(ev1), wall * 1e3) / e2e_steps], device=dev)
+    world = 1
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        world = pg.get_world_size()
+    e2e_ms = float(t.item())
     h2d = in_h.numel() * 2
     d2h = res_h.numel() * 2
     job_bytes = algorithmic_bytes(M, H, N_loc, wl["res"]) * world
-    how_out = ("the rank's output and updated residual written by the kernel straight into one pinned host buffer "
-               "(out= / residual_out= pinned host tensors)" if host_out else
-               "the rank's output and updated residual written into one device buffer and read back in one copy")
     return {"value": round(job_bytes / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
             "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
             "h2d_bytes_per_step_per_gpu": h2d, "d2h_bytes_per_step_per_gpu": d2h,
             "ms_per_step": round(e2e_ms, 6), "steps": e2e_steps,
-            "path": "fused_add_rmsnorm_matmul (public API) on every rank: x and residual in from one pinned host "
-                    f"buffer (one copy), {how_out}, synchronised every step; job bytes over the max-over-ranks time",
-            "device_outputs": {"value": round(job_bytes / (copy_ms / 1e3) / 1e9, 3), "unit": "GB/s",
-                               "ms_per_step": round(copy_ms, 6),
-                               "path": "the same, with the results written into one device buffer and read back "
-                                       "by one device-to-host copy"},
+            "path": "fused_add_rmsnorm_matmul (public API) on every rank: x and residual in from one pinned "
+                    "host buffer (one copy), the rank's output and updated residual written by the call into one "
+                    "device buffer (out= / residual_out=) and read back in one copy, synchronised every step; "
+                    "job bytes over the max-over-ranks time",
             "n_gpus_used": world}
 
 

@@ -628,21 +628,6 @@ extern "C" FQKV_API int fqkv_stream_capture_id(void* stream, unsigned long long*
   return 0;
 }
 
-extern "C" FQKV_API int fqkv_check_host_buffer(const void* p, int64_t bytes) {
-  if (!p) return fail(FQKV_ERR_NULL, "host buffer must be non-null");
-  if (bytes <= 0) return fail(FQKV_ERR_SHAPE, "host buffer size must be positive");
-  const char* last = static_cast<const char*>(p) + (bytes - 1);
-  for (const void* q : {p, static_cast<const void*>(last)}) {  // both ends lie in the allocation
-    cudaPointerAttributes a;
-    const cudaError_t e = cudaPointerGetAttributes(&a, q);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
-    if (a.type != cudaMemoryTypeHost || a.devicePointer != q)
-      return fail(FQKV_ERR_ALIGN, "host output buffer must be page-locked memory mapped at the same device address "
-                  "(e.g. a pinned tensor); pageable memory is not reachable from the GPU");
-  }
-  return 0;
-}
-
 extern "C" FQKV_API int fqkv_launch(const void* x, const void* residual, const void* rms_weight, int rms_weight_dtype,
                            const void* weight, void* out, void* residual_out, int64_t M, int64_t H, int64_t N,
                            int64_t ldx, int64_t ldr, int64_t ldw, int64_t ldo, int64_t ldro, float eps, int dtype,

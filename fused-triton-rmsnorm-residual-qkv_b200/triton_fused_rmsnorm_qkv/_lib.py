@@ -41,7 +41,6 @@ EXPORTED_SYMBOLS = (
     "fqkv_last_error",
     "fqkv_device_status",
     "fqkv_stream_capture_id",
-    "fqkv_check_host_buffer",
     "fqkv_test_set_wait_limit_ns",
     "fqkv_version",
 )
@@ -93,8 +92,6 @@ def load() -> ctypes.CDLL:
     lib.fqkv_test_set_wait_limit_ns.restype = i32
     lib.fqkv_stream_capture_id.argtypes = [vp, ctypes.POINTER(ctypes.c_ulonglong)]
     lib.fqkv_stream_capture_id.restype = i32
-    lib.fqkv_check_host_buffer.argtypes = [vp, i64]
-    lib.fqkv_check_host_buffer.restype = i32
     lib.fqkv_version.argtypes = []
     lib.fqkv_version.restype = i32
     lib.fqkv_launch_fp8w.argtypes = [vp, vp, vp, i32, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, f32,
@@ -153,12 +150,6 @@ def set_wait_limit_ns(ns: int) -> None:
     """Tests of the failure path: the bounded-wait limit of kernels launched from now on
     (current device); 0 restores the default of 1 s."""
     check(load().fqkv_test_set_wait_limit_ns(ns), "fqkv_test_set_wait_limit_ns")
-
-
-def check_host_buffer(ptr: int, nbytes: int) -> None:
-    """Raise unless [ptr, ptr + nbytes) is page-locked host memory the current device
-    reaches at the same address."""
-    check(load().fqkv_check_host_buffer(ptr, nbytes), "fqkv_check_host_buffer")
 
 
 def stream_capture_id(stream: int) -> int:

@@ -260,38 +260,6 @@ def _call(x2, r2, g, gcode, w, out2, rout2, M, H, N, ldx, ldr, ldw, ldo, ldro, e
         float(eps), dt, code, flags, ws.data_ptr() if ws is not None else None, ws_bytes, stream)
 
 
-# Schedules whose kernels write `out` and the updated residual with plain stores, which may
-# therefore target page-locked host memory (the others store through TMA tensor maps).
-_HOST_OUTPUT_SCHEDULES = (_lib.SCHED_DECODE, _lib.SCHED_GRID, _lib.SCHED_SIMT)
-_host_output_sched: dict[tuple, int] = {}
-
-
-def _span_bytes(t: torch.Tensor) -> int:
-    """Bytes from t's first element to the end of its last."""
-    return (1 + sum((n - 1) * st for n, st in zip(t.shape, t.stride()) if n > 0)) * t.element_size()
-
-
-def _check_host_outputs(tensors, x: torch.Tensor, M: int, H: int, N: int, schedule) -> None:
-    """Outputs in host memory: each must be page-locked and mapped at the same address for
-    the GPU, and the call's schedule one whose kernels store with plain stores (decode, grid
-    or simt: at most 64 rows)."""
-    code = _schedule_code(schedule)
-    index = x.get_device()
-    key = (M, H, N, x.dtype, index, code)
-    sched = _host_output_sched.get(key)
-    with torch.cuda.device(index):
-        if sched is None:
-            sched = code if code != _lib.SCHED_AUTO else schedule_info(M, H, N, x.dtype)["schedule"]
-            _host_output_sched[key] = sched
-        if sched not in _HOST_OUTPUT_SCHEDULES:
-            raise ValueError(f"outputs in host memory need the decode, grid or simt schedule; this call runs "
-                             f"{_lib.SCHEDULE_NAMES.get(sched, sched)} (M={M})")
-        for t in tensors:
-            if t.device.type != "cpu":
-                raise ValueError(f"an output on {t.device} does not match x on {x.device}")
-            _lib.check_host_buffer(t.data_ptr(), _span_bytes(t))
-
-
 def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, static_weights, out=None):
     assert x.is_cuda, "Fused kernel requires CUDA tensors"
     B, S, H = x.shape
@@ -304,30 +272,19 @@ def _fused(x, residual, rms_weight, weight, eps, *, residual_out, schedule, stat
         if residual.numel() != M * H:
             raise ValueError(f"residual must match x {tuple(x.shape)}, got {tuple(residual.shape)}")
         r2 = _rows(residual, M, H)
-    host_outputs = []
     if out is None:
         out = torch.empty(B, S, N_OUT, dtype=x.dtype, device=x.device)
-    else:
-        out_host = not out.is_cuda
-        if (out.shape != (B, S, N_OUT) or out.dtype != x.dtype or (not out_host and out.get_device() != x.get_device())
-                or out.stride(2) != 1 or (B > 1 and out.stride(0) != S * out.stride(1))):
-            raise ValueError(f"out must be a ({B}, {S}, {N_OUT}) {x.dtype} tensor on {x.device} (or in page-locked "
-                             "host memory) whose rows are uniformly strided with unit stride along N")
-        if out_host:
-            host_outputs.append(out)
+    elif (out.shape != (B, S, N_OUT) or out.dtype != x.dtype or out.get_device() != x.get_device()
+          or out.stride(2) != 1 or (B > 1 and out.stride(0) != S * out.stride(1))):
+        raise ValueError(f"out must be a ({B}, {S}, {N_OUT}) {x.dtype} tensor on {x.device} whose rows are "
+                         "uniformly strided with unit stride along N")
     rout2 = None
     if residual_out is not None:
-        rout_host = not residual_out.is_cuda
-        if (residual_out.numel() != M * H or residual_out.dtype != x.dtype
-                or (not rout_host and residual_out.get_device() != x.get_device())):
-            raise ValueError("residual_out must have the shape, dtype and device of x (or be in page-locked host memory)")
+        if residual_out.numel() != M * H or residual_out.dtype != x.dtype or residual_out.get_device() != x.get_device():
+            raise ValueError("residual_out must have the shape, dtype and device of x")
         rout2 = _rows(residual_out, M, H)
         if rout2.data_ptr() != residual_out.data_ptr() or rout2.stride(-1) != 1:
             raise ValueError("residual_out must be writable as M rows with unit stride along H")
-        if rout_host:
-            host_outputs.append(rout2)
-    if host_outputs:
-        _check_host_outputs(host_outputs, x, M, H, N_OUT, schedule)
     if static_weights is None:
         static_weights = _env_flag("FQKV_STATIC_WEIGHTS")
     _launch(x2, r2, rms_weight, weight, out, rout2, eps, schedule, static_weights, M)
@@ -360,11 +317,6 @@ def fused_rmsnorm_residual_matmul(
             (default: environment variable FQKV_STATIC_WEIGHTS).
         out: optional (B, S, N_OUT) tensor in x.dtype that receives the result (rows
             uniformly strided, unit stride along N) instead of a new allocation.
-            ``out`` and ``residual_out`` may also be page-locked (pinned) host tensors
-            when the call runs the decode, grid or simt schedule (at most 64 rows): the
-            kernel then writes the results straight into host memory, so a host that
-            wants them there needs no separate device-to-host copy (it synchronises the
-            stream before reading them).
 
     Returns:
         (B, S, N_OUT) tensor in x.dtype (``out`` when given).
@@ -391,9 +343,7 @@ def fused_add_rmsnorm_matmul(
     Returns ``(out, hidden)`` with ``hidden = x + residual`` computed once in fp32 and
     rounded to x.dtype (bit-identical to ``x + residual`` in PyTorch, baseline.py:48),
     or ``out`` alone when ``return_residual`` is False.  ``out`` and ``residual_out``
-    (with ``return_residual``) receive the two results instead of new allocations; either
-    may be a pinned host tensor on the decode, grid and simt schedules (see
-    ``fused_rmsnorm_residual_matmul``).
+    (with ``return_residual``) receive the two results instead of new allocations.
     """
     hidden = None
     if return_residual:

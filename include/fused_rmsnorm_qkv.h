@@ -184,15 +184,6 @@ FQKV_API int fqkv_test_set_wait_limit_ns(unsigned long long ns);
  * No counterpart in the reference (Triton launches need no scratch). */
 FQKV_API int fqkv_stream_capture_id(void* stream, unsigned long long* id);
 
-/* 0 when [p, p + bytes) is page-locked host memory that the current device reaches at the
- * same address (cudaPointerGetAttributes: host memory whose device pointer is p), else
- * FQKV_ERR_ALIGN with a message.  The decode and grid schedules (and SIMT) write `out` and
- * `residual_out` with plain stores, so such memory can receive their results directly: a
- * host that wants the results in host memory then needs no separate device-to-host copy.
- * Pageable memory is not reachable from the device and is rejected.  No counterpart in the
- * reference (its outputs are device tensors). */
-FQKV_API int fqkv_check_host_buffer(const void* p, int64_t bytes);
-
 /*
  * The op without a workspace, for callers that cannot allocate device memory when they
  * run it -- an inference engine's plugin whose enqueue step must not allocate, a runtime
