@@ -67,6 +67,10 @@ __host__ __device__ constexpr int f8_terms(bool bf16) { return decode_f8_terms(b
 constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
 constexpr int kGridBatch = 8;       // grid variant: 16-byte chunks per thread loaded before any is used
 constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
+// Up to this many rows (16-bit weights, MPAD = 16), the norm phase spreads each row's chunks
+// over all eight norm warps instead of giving each warp whole rows.
+constexpr int kSpreadMaxM = 2;
+static_assert(kNormWarps * kSpreadMaxM <= 16, "per-warp row sums of the spread norm phase fit rstd_s");
 
 struct Layout {
   uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, rscale, recvd, bars, tmem_slot, total;
@@ -119,7 +123,7 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
 }
 
-template <typename T, int MPAD, int NT, bool F8, bool GRID>
+template <typename T, int MPAD, int NT, bool F8, bool GRID, bool SPREAD>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmW, const DecodeParams p, const int stages) {
   extern __shared__ uint8_t smem_raw[];
@@ -377,7 +381,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rows costs one memory latency (M = 16: one pair per warp).  When that is all of the
     // warp's work (MPAD = 16 and at most 32 * kLoadBatch chunks per row), h also stays in
     // registers for pass 2.
-    const bool h_in_regs = !GRID && MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
+    // SPREAD (M <= kSpreadMaxM, 16-bit weights, cluster kernel): chunk j of each row in thread
+    // j % 256, so a single row's chunks do not all fall to one warp in either pass.
+    constexpr bool spread = SPREAD;
+    static_assert(!SPREAD || (!F8 && !GRID && MPAD == 16), "the spread norm phase: 16-bit cluster kernel, MPAD 16");
+    const bool h_in_regs = !GRID && !spread && MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
     uint4 hkeep[2][kLoadBatch];
     if constexpr (GRID) {
       // Whole rows: every CTA forms h = x + r over the entire row and its sum of squares
@@ -437,6 +445,52 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
           if (lane == 0) red[nw * MPAD + m] = ss;
         }
+      }
+    } else if (spread) {
+      // Each thread forms h of chunk j = et (+ 256) of every row; the warps' sums of squares
+      // go to rstd_s[warp * kSpreadMaxM + m] (free until the rows' rstd is formed) and the
+      // cluster exchange adds them in warp order.
+      uint64_t ssp[kSpreadMaxM];
+  #pragma unroll
+      for (int m = 0; m < kSpreadMaxM; ++m) ssp[m] = 0ull;
+      for (int j0 = 0; j0 < nchunk; j0 += 2 * kNormThreads) {
+        uint4 xv[2][kSpreadMaxM], rv[2][kSpreadMaxM];
+  #pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const int j = j0 + et + kNormThreads * b;
+          const int64_t k = k_lo + (int64_t)j * 8;
+  #pragma unroll
+          for (int m = 0; m < kSpreadMaxM; ++m) {
+            xv[b][m] = rv[b][m] = make_uint4(0, 0, 0, 0);
+            if (m < p.M && j < nchunk && k < p.H) {
+              xv[b][m] = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)m * p.ldx + k));
+              if (p.r) rv[b][m] = __ldg(reinterpret_cast<const uint4*>(p.r + (int64_t)m * p.ldr + k));
+            }
+          }
+        }
+  #pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const int j = j0 + et + kNormThreads * b;
+          const int64_t k = k_lo + (int64_t)j * 8;
+  #pragma unroll
+          for (int m = 0; m < kSpreadMaxM; ++m) {
+            if (m < p.M && j < nchunk) {  // chunks past the end of the row hold zeros
+              const uint4 hv = p.r ? add8_rn<T>(xv[b][m], rv[b][m]) : xv[b][m];
+              ssp[m] = sumsq8_f2<T>(hv, ssp[m]);
+              if (write_res && k < p.H) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
+              *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
+            }
+          }
+        }
+      }
+  #pragma unroll
+      for (int m = 0; m < kSpreadMaxM; ++m) {
+        float lo, hi;
+        f2_unpack(ssp[m], lo, hi);
+        float ss = lo + hi;
+  #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) rstd_s[nw * kSpreadMaxM + m] = ss;
       }
     } else {
       for (int m0 = nw; m0 < MPAD; m0 += 2 * kNormWarps) {
@@ -521,11 +575,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Publish this CTA's per-row partial sums into slot `rank` of every CTA: each st.async
       // counts its 4 bytes on the receiving CTA's sum_bar.
       if (warp == 2) {
+        float part_m = 0.f;  // spread: this lane's row (m = lane < M), summed over the warps in order
+        if (spread && lane < p.M)
+          for (int w = 0; w < kNormWarps; ++w) part_m += rstd_s[w * kSpreadMaxM + lane];
         for (uint32_t c = 0; c < C; ++c) {
           const uint32_t bar_c = mapa_shared(smem_u32(sum_bar), c);
           for (int m = lane; m < MPAD; m += 32)
-            st_async_f32(mapa_shared(smem_u32(&red[rank * MPAD + m]), c), rowp[m], bar_c);
+            st_async_f32(mapa_shared(smem_u32(&red[rank * MPAD + m]), c), spread ? part_m : rowp[m], bar_c);
         }
+        if constexpr (SPREAD) __syncwarp();  // every lane has read the per-warp sums before rstd_s is overwritten
       }
       ok = mbar_wait<true>(sum_bar, 0);
       for (int m = et; m < MPAD; m += kNormThreads) {
@@ -633,6 +691,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         pass2_f8(std::integral_constant<int, kLoadBatch>{}, std::true_type{});
       else
         pass2_f8(std::integral_constant<int, kF8Batch>{}, std::false_type{});
+    } else if (spread) {
+      // As in pass 1: chunk j of every row in thread j % 256 (h from the operand buffer).
+      for (int j = et; j < nchunk; j += kNormThreads) {
+        if (k_lo + (int64_t)j * 8 >= p.H) continue;  // past the end of the row: stays zero
+        uint64_t g2[4];
+        load_g2(j, g2);
+  #pragma unroll
+        for (int m = 0; m < kSpreadMaxM; ++m) {
+          if (m < p.M) {
+            uint4* dst = reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
+            *dst = normalize8_f2<T>(*dst, f2_pack(rstd_s[m], rstd_s[m]), g2);
+          }
+        }
+      }
     } else if (h_in_regs) {
       if (nw < p.M) {  // rows nw and nw + 8; padding rows are skipped (warp-uniform)
         const bool live1 = nw + kNormWarps < p.M;
@@ -935,9 +1007,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   FQKV_TRACE_END();
 }
 
-template <int MPAD, int NT, bool F8, bool GRID = false>
+template <int MPAD, int NT, bool F8, bool GRID = false, bool SPREAD = false>
 auto kernel_ptr(bool bf16) {
-  return bf16 ? decode_kernel<__nv_bfloat16, MPAD, NT, F8, GRID> : decode_kernel<__half, MPAD, NT, F8, GRID>;
+  return bf16 ? decode_kernel<__nv_bfloat16, MPAD, NT, F8, GRID, SPREAD>
+              : decode_kernel<__half, MPAD, NT, F8, GRID, SPREAD>;
 }
 
 using KernelFn = void (*)(CUtensorMap, DecodeParams, int);
@@ -962,6 +1035,18 @@ KernelFn pick_kernel_t(int mpad, int nt, bool bf16) {
 
 KernelFn pick_kernel(int mpad, int nt, bool bf16, bool f8) {
   return f8 ? pick_kernel_t<true>(mpad, nt, bf16) : pick_kernel_t<false>(mpad, nt, bf16);
+}
+
+// The cluster kernel with the spread norm phase: 16-bit weights, MPAD 16, M <= kSpreadMaxM.
+KernelFn pick_spread_kernel(int nt, bool bf16) {
+  switch (nt) {
+    case 1: return kernel_ptr<16, 1, false, false, true>(bf16);
+    case 2: return kernel_ptr<16, 2, false, false, true>(bf16);
+    case 3: return kernel_ptr<16, 3, false, false, true>(bf16);
+    case 4: return kernel_ptr<16, 4, false, false, true>(bf16);
+    case 5: return kernel_ptr<16, 5, false, false, true>(bf16);
+    default: return nullptr;
+  }
 }
 
 // Grid variant: 16-bit weights, MPAD 16, 1 to 5 tiles per CTA.
@@ -1174,7 +1259,12 @@ int decode_grid_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg
 
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream) {
-  KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16) : pick_kernel(c.mpad, c.nt, bf16, c.f8 != 0);
+  // Rows up to kSpreadMaxM: the norm phase spread over all eight norm warps (measured on B200,
+  // graph-timed: Llama-3-8B M = 1 11.99 -> 11.69 us, Llama-3-70B M = 1 33.3 -> 30.7 us).
+  const bool spread = !c.grid && !c.f8 && c.mpad == 16 && p.M <= kSpreadMaxM;
+  KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16)
+               : spread ? pick_spread_kernel(c.nt, bf16)
+                        : pick_kernel(c.mpad, c.nt, bf16, c.f8 != 0);
   if (!k) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(k), c.smem);
   if (e != cudaSuccess) return e;
