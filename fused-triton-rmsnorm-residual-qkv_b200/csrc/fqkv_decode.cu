@@ -68,9 +68,12 @@ constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded be
 constexpr int kGridBatch = 8;       // grid variant: 16-byte chunks per thread loaded before any is used
 constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
 // Up to this many rows (16-bit weights, MPAD = 16), the norm phase spreads each row's chunks
-// over all eight norm warps instead of giving each warp whole rows.
-constexpr int kSpreadMaxM = 2;
-static_assert(kNormWarps * kSpreadMaxM <= 16, "per-warp row sums of the spread norm phase fit rstd_s");
+// over several norm warps instead of giving each warp whole rows.
+constexpr int kSpreadMaxM = 4;
+static_assert(kNormWarps <= 16, "the spread norm phase's per-warp row sums fit rstd_s");
+// log2 of the norm threads per row in the spread norm phase: all 256 for one row, 128 for
+// two, 64 for three or four (a whole number of warps per row).
+__host__ __device__ constexpr int spread_shift(int M) { return M == 1 ? 8 : M == 2 ? 7 : 6; }
 
 struct Layout {
   uint32_t ring, stage_bytes, normed, gain, red, rowp, rstd, rscale, recvd, bars, tmem_slot, total;
@@ -381,8 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rows costs one memory latency (M = 16: one pair per warp).  When that is all of the
     // warp's work (MPAD = 16 and at most 32 * kLoadBatch chunks per row), h also stays in
     // registers for pass 2.
-    // SPREAD (M <= kSpreadMaxM, 16-bit weights, cluster kernel): chunk j of each row in thread
-    // j % 256, so a single row's chunks do not all fall to one warp in either pass.
+    // SPREAD (M <= kSpreadMaxM, 16-bit weights, cluster kernel): each row's chunks over 256 / M
+    // (rounded down to a power of two) threads, so they do not all fall to one warp.
     constexpr bool spread = SPREAD;
     static_assert(!SPREAD || (!F8 && !GRID && MPAD == 16), "the spread norm phase: 16-bit cluster kernel, MPAD 16");
     const bool h_in_regs = !GRID && !spread && MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
@@ -447,51 +450,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (spread) {
-      // Each thread forms h of chunk j = et (+ 256) of every row; the warps' sums of squares
-      // go to rstd_s[warp * kSpreadMaxM + m] (free until the rows' rstd is formed) and the
-      // cluster exchange adds them in warp order.
-      uint64_t ssp[kSpreadMaxM];
-  #pragma unroll
-      for (int m = 0; m < kSpreadMaxM; ++m) ssp[m] = 0ull;
-      for (int j0 = 0; j0 < nchunk; j0 += 2 * kNormThreads) {
-        uint4 xv[2][kSpreadMaxM], rv[2][kSpreadMaxM];
+      // Row m = et / tpr, its chunks j = et % tpr (+ tpr, ...): 256, 128 or 64 threads per row
+      // for M = 1, 2 or 3-4.  Each warp serves one row; the warps' sums of squares go to
+      // rstd_s[warp] (free until the rows' rstd is formed), and the cluster exchange adds a
+      // row's warps in order.
+      const int shift = spread_shift(p.M), tpr = 1 << shift;
+      const int m = et >> shift, jj = et & (tpr - 1);
+      const bool row_live = m < p.M;
+      uint64_t ssp = 0ull;
+      for (int j0 = jj; j0 < nchunk; j0 += 2 * tpr) {
+        uint4 xv[2], rv[2];
   #pragma unroll
         for (int b = 0; b < 2; ++b) {
-          const int j = j0 + et + kNormThreads * b;
+          const int j = j0 + tpr * b;
           const int64_t k = k_lo + (int64_t)j * 8;
-  #pragma unroll
-          for (int m = 0; m < kSpreadMaxM; ++m) {
-            xv[b][m] = rv[b][m] = make_uint4(0, 0, 0, 0);
-            if (m < p.M && j < nchunk && k < p.H) {
-              xv[b][m] = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)m * p.ldx + k));
-              if (p.r) rv[b][m] = __ldg(reinterpret_cast<const uint4*>(p.r + (int64_t)m * p.ldr + k));
-            }
+          xv[b] = rv[b] = make_uint4(0, 0, 0, 0);
+          if (row_live && j < nchunk && k < p.H) {
+            xv[b] = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)m * p.ldx + k));
+            if (p.r) rv[b] = __ldg(reinterpret_cast<const uint4*>(p.r + (int64_t)m * p.ldr + k));
           }
         }
   #pragma unroll
         for (int b = 0; b < 2; ++b) {
-          const int j = j0 + et + kNormThreads * b;
+          const int j = j0 + tpr * b;
           const int64_t k = k_lo + (int64_t)j * 8;
-  #pragma unroll
-          for (int m = 0; m < kSpreadMaxM; ++m) {
-            if (m < p.M && j < nchunk) {  // chunks past the end of the row hold zeros
-              const uint4 hv = p.r ? add8_rn<T>(xv[b][m], rv[b][m]) : xv[b][m];
-              ssp[m] = sumsq8_f2<T>(hv, ssp[m]);
-              if (write_res && k < p.H) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
-              *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
-            }
+          if (row_live && j < nchunk) {  // chunks past the end of the row hold zeros
+            const uint4 hv = p.r ? add8_rn<T>(xv[b], rv[b]) : xv[b];
+            ssp = sumsq8_f2<T>(hv, ssp);
+            if (write_res && k < p.H) *reinterpret_cast<uint4*>(p.rout + (int64_t)m * p.ldro + k) = hv;
+            *reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7)) = hv;
           }
         }
       }
+      float lo, hi;
+      f2_unpack(ssp, lo, hi);
+      float ss = lo + hi;
   #pragma unroll
-      for (int m = 0; m < kSpreadMaxM; ++m) {
-        float lo, hi;
-        f2_unpack(ssp[m], lo, hi);
-        float ss = lo + hi;
-  #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) rstd_s[nw * kSpreadMaxM + m] = ss;
-      }
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) rstd_s[nw] = ss;
     } else {
       for (int m0 = nw; m0 < MPAD; m0 += 2 * kNormWarps) {
         uint64_t ss2[2] = {0ull, 0ull};  // fp32 pairs: even / odd elements
@@ -575,9 +571,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Publish this CTA's per-row partial sums into slot `rank` of every CTA: each st.async
       // counts its 4 bytes on the receiving CTA's sum_bar.
       if (warp == 2) {
-        float part_m = 0.f;  // spread: this lane's row (m = lane < M), summed over the warps in order
-        if (spread && lane < p.M)
-          for (int w = 0; w < kNormWarps; ++w) part_m += rstd_s[w * kSpreadMaxM + lane];
+        float part_m = 0.f;  // spread: this lane's row (m = lane < M), its warps' sums in order
+        if (spread && lane < p.M) {
+          const int wpr = 1 << (spread_shift(p.M) - 5);  // warps per row
+          for (int w = lane * wpr; w < (lane + 1) * wpr; ++w) part_m += rstd_s[w];
+        }
         for (uint32_t c = 0; c < C; ++c) {
           const uint32_t bar_c = mapa_shared(smem_u32(sum_bar), c);
           for (int m = lane; m < MPAD; m += 32)
@@ -692,17 +690,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       else
         pass2_f8(std::integral_constant<int, kF8Batch>{}, std::false_type{});
     } else if (spread) {
-      // As in pass 1: chunk j of every row in thread j % 256 (h from the operand buffer).
-      for (int j = et; j < nchunk; j += kNormThreads) {
-        if (k_lo + (int64_t)j * 8 >= p.H) continue;  // past the end of the row: stays zero
-        uint64_t g2[4];
-        load_g2(j, g2);
-  #pragma unroll
-        for (int m = 0; m < kSpreadMaxM; ++m) {
-          if (m < p.M) {
-            uint4* dst = reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
-            *dst = normalize8_f2<T>(*dst, f2_pack(rstd_s[m], rstd_s[m]), g2);
-          }
+      // As in pass 1: row et / tpr, chunks et % tpr (+ tpr, ...); h from the operand buffer.
+      const int shift = spread_shift(p.M), tpr = 1 << shift;
+      const int m = et >> shift;
+      if (m < p.M) {
+        const uint64_t rs2 = f2_pack(rstd_s[m], rstd_s[m]);
+        for (int j = et & (tpr - 1); j < nchunk; j += tpr) {
+          if (k_lo + (int64_t)j * 8 >= p.H) continue;  // past the end of the row: stays zero
+          uint64_t g2[4];
+          load_g2(j, g2);
+          uint4* dst = reinterpret_cast<uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
+          *dst = normalize8_f2<T>(*dst, rs2, g2);
         }
       }
     } else if (h_in_regs) {
@@ -1260,7 +1258,8 @@ int decode_grid_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream) {
   // Rows up to kSpreadMaxM: the norm phase spread over all eight norm warps (measured on B200,
-  // graph-timed: Llama-3-8B M = 1 11.99 -> 11.69 us, Llama-3-70B M = 1 33.3 -> 30.7 us).
+  // graph-timed: Llama-3-8B M = 1 / 2 11.84 / 11.92 -> 11.64 / 11.59 us, Llama-3-70B M = 1
+  // 33.4 -> 30.6 us).
   const bool spread = !c.grid && !c.f8 && c.mpad == 16 && p.M <= kSpreadMaxM;
   KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16)
                : spread ? pick_spread_kernel(c.nt, bf16)

@@ -120,9 +120,11 @@ SCHEDULE_CASES = [
     # M, H, N, schedules that can take it
     (1, 512, 640, ("simt", "decode", "split", "prefill")),
     (5, 264, 200, ("simt", "decode", "split", "prefill")),     # H % 64 != 0, ragged N
-    (2, 264, 200, ("decode", "split")),       # the spread norm phase (M <= 2), ragged K and N
+    (2, 264, 200, ("decode", "split")),       # the spread norm phase (M <= 4), ragged K and N
     (1, 4104, 700, ("decode",)),              # spread, a K slice ending 8 elements into a k-block
     (2, 8192, 1024, ("decode",)),             # spread, long rows
+    (3, 264, 200, ("decode",)),               # spread over 64 threads per row, a row slot unused
+    (4, 4104, 700, ("decode",)),              # spread, four rows, ragged K
     (16, 1024, 1280, ("simt", "decode", "split", "prefill")),
     (33, 512, 768, ("simt", "decode", "split", "prefill")),
     (64, 2048, 2560, ("simt", "decode", "split", "prefill")),
