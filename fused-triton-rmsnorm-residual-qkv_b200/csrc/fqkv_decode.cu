@@ -63,6 +63,7 @@ constexpr int kWTileBytes = kTileRows * 128;
 // take one MPAD x 128-byte region each per two k-blocks.
 constexpr int kF8Batch = 8;                   // e4m3 weights: 16-byte chunks per lane and row in pass 2
 constexpr int kF8Max = kF8Batch * 32 / 8;     // k-blocks of one CTA's K slice at most (pass 2 in registers)
+constexpr int kF8SpreadPer = kF8Max * 8 / 64;  // e4m3, spread pass 2: chunks per thread at most (>= 64 per row)
 __host__ __device__ constexpr int f8_terms(bool bf16) { return decode_f8_terms(bf16); }
 constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
 constexpr int kGridBatch = 8;       // grid variant: 16-byte chunks per thread loaded before any is used
@@ -384,10 +385,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rows costs one memory latency (M = 16: one pair per warp).  When that is all of the
     // warp's work (MPAD = 16 and at most 32 * kLoadBatch chunks per row), h also stays in
     // registers for pass 2.
-    // SPREAD (M <= kSpreadMaxM, 16-bit weights, cluster kernel): each row's chunks over 256 / M
-    // (rounded down to a power of two) threads, so they do not all fall to one warp.
+    // SPREAD (M <= kSpreadMaxM, cluster kernel): each row's chunks over 256 / M (rounded down to
+    // a power of two) threads, so they do not all fall to one warp.
     constexpr bool spread = SPREAD;
-    static_assert(!SPREAD || (!F8 && !GRID && MPAD == 16), "the spread norm phase: 16-bit cluster kernel, MPAD 16");
+    static_assert(!SPREAD || (!GRID && MPAD == 16), "the spread norm phase: cluster kernel, MPAD 16");
     const bool h_in_regs = !GRID && !spread && MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
     uint4 hkeep[2][kLoadBatch];
     if constexpr (GRID) {
@@ -685,10 +686,61 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
-      if (h_in_regs)
+      if constexpr (SPREAD) {
+        // Spread (as in pass 1: row et / tpr, chunks et % tpr + tpr * b): every thread
+        // normalises its chunks into registers and takes their largest magnitude; the row's
+        // warps meet in shared memory for the row's power of two, and only after that barrier,
+        // when every h of the slice has been read, are the terms written over the buffer.
+        const int shift = spread_shift(p.M), tpr = 1 << shift;
+        const int m = et >> shift, jj = et & (tpr - 1);
+        const bool row_live = m < p.M;
+        const uint64_t rs2 = row_live ? f2_pack(rstd_s[m], rstd_s[m]) : 0ull;
+        uint4 o[kF8SpreadPer];
+        uint32_t mx = 0u;
+  #pragma unroll
+        for (int b = 0; b < kF8SpreadPer; ++b) {
+          o[b] = make_uint4(0, 0, 0, 0);
+          const int j = jj + tpr * b;
+          if (row_live && j < nchunk && k_lo + (int64_t)j * 8 < p.H) {
+            uint64_t g2[4];
+            load_g2(j, g2);
+            const uint4 hv = *reinterpret_cast<const uint4*>(normed + (j >> 3) * (MPAD * 128) + sw128_offset(m, j & 7));
+            o[b] = normalize8_f2<T>(hv, rs2, g2);
+            mx = absmax8_bits(o[b], mx);
+          }
+        }
+        uint32_t* wmax = reinterpret_cast<uint32_t*>(rowp);  // per-warp maxima (rowp is unused when spread)
+        const uint32_t mxw = __reduce_max_sync(0xffffffffu, max(mx & 0xFFFFu, mx >> 16));
+        if (lane == 0) wmax[nw] = mxw;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (row_live) {
+          uint32_t mxb = 0u;
+          const int wpr = 1 << (shift - 5);  // warps per row
+          for (int w = m * wpr; w < (m + 1) * wpr; ++w) mxb = max(mxb, wmax[w]);
+          const float mxf = Elem<T>::to_f((uint16_t)mxb);
+          // mx in [2^e, 2^(e+1)): scale by 2^(7 - e).
+          const int e = mxf > 0.f ? (int)((__float_as_uint(mxf) >> 23) & 0xFFu) - 127 : 7;
+          const int sh = min(max(7 - e, -100), 100);
+          const float up = __uint_as_float((uint32_t)(127 + sh) << 23);
+          if (jj == 0) rscale[m] = __uint_as_float((uint32_t)(127 - sh) << 23);
+          const int nchunk16 = (nchunk + 15) & ~15;  // the terms of whole 128 K, zeros beyond the slice
+  #pragma unroll
+          for (int b = 0; b < kF8SpreadPer; ++b) {
+            const int j = jj + tpr * b;
+            if (j < nchunk16) {
+              uint2 t8[kTerms];
+              split_e4m3<T, kTerms>(o[b], up, t8);
+  #pragma unroll
+              for (int t = 0; t < kTerms; ++t)
+                *reinterpret_cast<uint2*>(normed + term_off(m, j) + t * (MPAD * 128)) = t8[t];
+            }
+          }
+        }
+      } else if (h_in_regs) {
         pass2_f8(std::integral_constant<int, kLoadBatch>{}, std::true_type{});
-      else
+      } else {
         pass2_f8(std::integral_constant<int, kF8Batch>{}, std::false_type{});
+      }
     } else if (spread) {
       // As in pass 1: row et / tpr, chunks et % tpr (+ tpr, ...); h from the operand buffer.
       const int shift = spread_shift(p.M), tpr = 1 << shift;
@@ -1035,16 +1087,21 @@ KernelFn pick_kernel(int mpad, int nt, bool bf16, bool f8) {
   return f8 ? pick_kernel_t<true>(mpad, nt, bf16) : pick_kernel_t<false>(mpad, nt, bf16);
 }
 
-// The cluster kernel with the spread norm phase: 16-bit weights, MPAD 16, M <= kSpreadMaxM.
-KernelFn pick_spread_kernel(int nt, bool bf16) {
+// The cluster kernel with the spread norm phase: MPAD 16, M <= kSpreadMaxM.
+template <bool F8>
+KernelFn pick_spread_kernel_t(int nt, bool bf16) {
   switch (nt) {
-    case 1: return kernel_ptr<16, 1, false, false, true>(bf16);
-    case 2: return kernel_ptr<16, 2, false, false, true>(bf16);
-    case 3: return kernel_ptr<16, 3, false, false, true>(bf16);
-    case 4: return kernel_ptr<16, 4, false, false, true>(bf16);
-    case 5: return kernel_ptr<16, 5, false, false, true>(bf16);
+    case 1: return kernel_ptr<16, 1, F8, false, true>(bf16);
+    case 2: return kernel_ptr<16, 2, F8, false, true>(bf16);
+    case 3: return kernel_ptr<16, 3, F8, false, true>(bf16);
+    case 4: return kernel_ptr<16, 4, F8, false, true>(bf16);
+    case 5: return kernel_ptr<16, 5, F8, false, true>(bf16);
     default: return nullptr;
   }
+}
+
+KernelFn pick_spread_kernel(int nt, bool bf16, bool f8) {
+  return f8 ? pick_spread_kernel_t<true>(nt, bf16) : pick_spread_kernel_t<false>(nt, bf16);
 }
 
 // Grid variant: 16-bit weights, MPAD 16, 1 to 5 tiles per CTA.
@@ -1260,9 +1317,9 @@ cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const D
   // Rows up to kSpreadMaxM: the norm phase spread over all eight norm warps (measured on B200,
   // graph-timed: Llama-3-8B M = 1 / 2 11.84 / 11.92 -> 11.64 / 11.59 us, Llama-3-70B M = 1
   // 33.4 -> 30.6 us).
-  const bool spread = !c.grid && !c.f8 && c.mpad == 16 && p.M <= kSpreadMaxM;
+  const bool spread = !c.grid && c.mpad == 16 && p.M <= kSpreadMaxM;
   KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16)
-               : spread ? pick_spread_kernel(c.nt, bf16)
+               : spread ? pick_spread_kernel(c.nt, bf16, c.f8 != 0)
                         : pick_kernel(c.mpad, c.nt, bf16, c.f8 != 0);
   if (!k) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(k), c.smem);

@@ -49,9 +49,17 @@ def test_gate_up_fp8w(M):
     run_fp8(M, 4096, 28672, torch.bfloat16, seed=60 + M)
 
 
-@pytest.mark.parametrize("M,H,N", [(5, 272, 200), (33, 512, 768), (1, 1024, 1280)])
+@pytest.mark.parametrize("M,H,N", [(5, 272, 200), (33, 512, 768), (1, 1024, 1280),
+                                   (2, 272, 200), (3, 1040, 700), (4, 8192, 1024)])  # the spread norm phase
 def test_ragged_fp8w(M, H, N):
     run_fp8(M, H, N, torch.bfloat16, seed=M + H)
+
+
+@pytest.mark.parametrize("M", [1, 2, 4])
+def test_spread_fp8w_fp16_three_terms(M):
+    """fp16: three e4m3 terms per value, whose regions reach past their own 128 K of the
+    16-bit buffer they overwrite; the spread norm phase (M <= 4) reads every h first."""
+    run_fp8(M, 1040, 1280, torch.float16, seed=80 + M)
 
 
 def test_fp8w_rejects_prefill_sizes():
@@ -68,13 +76,15 @@ def test_llama3_8b_decode_fp8w_fp16_sizes(M):
     run_fp8(M, 4096, 6144, torch.float16, seed=70 + M)
 
 
+@pytest.mark.parametrize("M", [16, 1, 4])
 @pytest.mark.parametrize("dtype,min_equal", [(torch.bfloat16, 0.99), (torch.float16, 0.97)])
-def test_fp8w_term_split_is_exact(dtype, min_equal):
+def test_fp8w_term_split_is_exact(dtype, min_equal, M):
     """The activations' e4m3 terms hold the normalised values exactly, so the kernel differs
     from the fp64 oracle only by its fp32 accumulation: nearly every output is bit-identical,
     and none is further away than one unit in the last place plus the fp32 rounding of a
-    4096-term sum (1e-5 of the largest output; it dominates only for outputs near zero)."""
-    M, H, N = 16, 4096, 6144
+    4096-term sum (1e-5 of the largest output; it dominates only for outputs near zero).
+    M = 1 and 4 run the spread norm phase."""
+    H, N = 4096, 6144
     x, r, g, w = make_case(M, H, N, dtype, seed=91)
     w8, scale = quantize_weight_e4m3(w)
     out, _ = fused_add_rmsnorm_matmul_fp8w(x.cuda()[None], r.cuda()[None], g.cuda(), w8.cuda(), scale.cuda(), 1e-5)
