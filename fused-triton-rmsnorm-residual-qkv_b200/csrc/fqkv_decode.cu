@@ -385,11 +385,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rows costs one memory latency (M = 16: one pair per warp).  When that is all of the
     // warp's work (MPAD = 16 and at most 32 * kLoadBatch chunks per row), h also stays in
     // registers for pass 2.
-    // SPREAD (M <= kSpreadMaxM): each row's chunks over 256 / M (rounded down to a power of
-    // two) threads, so they do not all fall to one warp (the grid variant's pass 1 reads whole
-    // rows spread over all threads anyway; it takes the spread pass 2).
+    // SPREAD (M <= kSpreadMaxM, cluster kernel): each row's chunks over 256 / M (rounded down to
+    // a power of two) threads, so they do not all fall to one warp.
     constexpr bool spread = SPREAD;
-    static_assert(!SPREAD || MPAD == 16, "the spread norm phase: MPAD 16");
+    static_assert(!SPREAD || (!GRID && MPAD == 16), "the spread norm phase: cluster kernel, MPAD 16");
     const bool h_in_regs = !GRID && !spread && MPAD == 2 * kNormWarps && nchunk <= 32 * kLoadBatch;
     uint4 hkeep[2][kLoadBatch];
     if constexpr (GRID) {
@@ -1106,20 +1105,15 @@ KernelFn pick_spread_kernel(int nt, bool bf16, bool f8) {
 }
 
 // Grid variant: 16-bit weights, MPAD 16, 1 to 5 tiles per CTA.
-template <bool SPREAD>
-KernelFn pick_grid_kernel_t(int nt, bool bf16) {
+KernelFn pick_grid_kernel(int nt, bool bf16) {
   switch (nt) {
-    case 1: return kernel_ptr<16, 1, false, true, SPREAD>(bf16);
-    case 2: return kernel_ptr<16, 2, false, true, SPREAD>(bf16);
-    case 3: return kernel_ptr<16, 3, false, true, SPREAD>(bf16);
-    case 4: return kernel_ptr<16, 4, false, true, SPREAD>(bf16);
-    case 5: return kernel_ptr<16, 5, false, true, SPREAD>(bf16);
+    case 1: return kernel_ptr<16, 1, false, true>(bf16);
+    case 2: return kernel_ptr<16, 2, false, true>(bf16);
+    case 3: return kernel_ptr<16, 3, false, true>(bf16);
+    case 4: return kernel_ptr<16, 4, false, true>(bf16);
+    case 5: return kernel_ptr<16, 5, false, true>(bf16);
     default: return nullptr;
   }
-}
-
-KernelFn pick_grid_kernel(int nt, bool bf16, bool spread = false) {
-  return spread ? pick_grid_kernel_t<true>(nt, bf16) : pick_grid_kernel_t<false>(nt, bf16);
 }
 
 cudaLaunchConfig_t base_config(const DecodeConfig& c, int tiles, cudaLaunchAttribute* attr, int* na) {
@@ -1323,8 +1317,8 @@ cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const D
   // Rows up to kSpreadMaxM: the norm phase spread over all eight norm warps (measured on B200,
   // graph-timed: Llama-3-8B M = 1 / 2 11.84 / 11.92 -> 11.64 / 11.59 us, Llama-3-70B M = 1
   // 33.4 -> 30.6 us).
-  const bool spread = c.mpad == 16 && p.M <= kSpreadMaxM;
-  KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16, spread)
+  const bool spread = !c.grid && c.mpad == 16 && p.M <= kSpreadMaxM;
+  KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16)
                : spread ? pick_spread_kernel(c.nt, bf16, c.f8 != 0)
                         : pick_kernel(c.mpad, c.nt, bf16, c.f8 != 0);
   if (!k) return cudaErrorInvalidValue;
