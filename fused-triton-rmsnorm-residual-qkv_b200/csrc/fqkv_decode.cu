@@ -68,8 +68,8 @@ __host__ __device__ constexpr int f8_terms(bool bf16) { return decode_f8_terms(b
 constexpr int kLoadBatch = 4;       // 16-byte chunks per lane and row loaded before any is used
 constexpr int kGridBatch = 8;       // grid variant: 16-byte chunks per thread loaded before any is used
 constexpr int kGainChunks = 2;      // gain chunks per thread: K slices up to 2 * 256 * 8 elements
-// Up to this many rows (16-bit weights, MPAD = 16), the norm phase spreads each row's chunks
-// over several norm warps instead of giving each warp whole rows.
+// Up to this many rows (cluster kernel, MPAD = 16, 16-bit or e4m3 weights), the norm phase
+// spreads each row's chunks over several norm warps instead of giving each warp whole rows.
 constexpr int kSpreadMaxM = 4;
 static_assert(kNormWarps <= 16, "the spread norm phase's per-warp row sums fit rstd_s");
 // log2 of the norm threads per row in the spread norm phase: all 256 for one row, 128 for
@@ -1314,9 +1314,10 @@ int decode_grid_pick_config(int M, int H, int N, int sm_count, DecodeConfig* cfg
 
 cudaError_t launch_decode(const DecodeConfig& c, const CUtensorMap& tmW, const DecodeParams& p, bool bf16, bool pdl,
                           cudaStream_t stream) {
-  // Rows up to kSpreadMaxM: the norm phase spread over all eight norm warps (measured on B200,
-  // graph-timed: Llama-3-8B M = 1 / 2 11.84 / 11.92 -> 11.64 / 11.59 us, Llama-3-70B M = 1
-  // 33.4 -> 30.6 us).
+  // Rows up to kSpreadMaxM: the norm phase spread over the norm warps (measured on B200,
+  // graph-timed: Llama-3-8B M = 1 / 4 11.99 / 12.08 -> 11.71 / 11.87 us, Llama-3-70B M = 1
+  // 33.4 -> 30.8 us, e4m3 M = 1 9.86 -> 9.01 us).  The grid variant keeps one warp per row:
+  // its pass 1 already reads whole rows over all threads, and the spread pass 2 was slower.
   const bool spread = !c.grid && c.mpad == 16 && p.M <= kSpreadMaxM;
   KernelFn k = c.grid ? pick_grid_kernel(c.nt, bf16)
                : spread ? pick_spread_kernel(c.nt, bf16, c.f8 != 0)
