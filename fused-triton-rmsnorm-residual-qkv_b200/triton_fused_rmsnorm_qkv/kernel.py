@@ -18,8 +18,9 @@ library chooses one of its kernel families from (M, H, N, SM count):
 * ``grid``    (M <= 8): the same fused kernel without clusters, so that its CTAs cover
   nearly every SM.  Each CTA reads the whole activation rows, and the CTA that finishes a
   tile last sums the partial tiles through a zero-filled workspace this module keeps per
-  device and stream.  Chosen automatically for M <= ``_GRID_AUTO_MAX_M`` when it cuts the
-  weight bytes per CTA well below the cluster kernel's (``_grid_preferred``).
+  device and stream.  Chosen automatically for M <= ``_GRID_AUTO_MAX_M`` only when it cuts
+  the weight bytes per CTA far below the cluster kernel's (``_grid_preferred``); no measured
+  model shape qualifies, so in practice it runs when forced (``schedule="grid"``).
 * ``split``   (M <= 64 when no decode configuration fits the device, or when forced; up
   to M = 128): norm pre-pass + a stream-K swap-AB GEMM reading the normalised rows by TMA.
 * ``prefill`` (M > 64): norm pre-pass + persistent 128 x BN tcgen05 GEMM.
@@ -57,12 +58,15 @@ _ws_bytes: dict[tuple, int] = {}
 
 # The automatic choice of the grid schedule: at most this many rows (every CTA reads whole
 # rows, which stops paying beyond a few), and at most this fraction of the cluster kernel's
-# weight bytes per CTA.  Measured on B200, graph-timed, M = 1 (cluster -> grid, us):
-# Qwen2-7B 12.70 -> 11.25 (fraction 0.74); Llama-3-8B 12.04 -> 14.0 (0.85); Llama-3-70B
-# 32.8 -> 33.9 (0.88); the gate/up weight 42.9 -> 42.6 (1.0, the same configuration).  At
-# M = 4 the Qwen2-7B shape is 12.9 against 13.2 us.
+# weight bytes per CTA.  Since the cluster kernel spreads the norm phase of one to four rows
+# over all its norm warps, it beats the grid variant on every measured shape (B200,
+# graph-timed, M = 1 / 2, cluster against grid, us): Qwen2-7B 10.50 / 10.91 against 11.60 /
+# 12.23 (bytes fraction 0.74), Llama-3-8B 11.69 / 11.63 against 14.32 / 14.94 (0.85),
+# Llama-3-70B 30.64 / 31.16 against 33.18 / 35.77 (0.88).  The fraction is therefore set
+# below all of them: the grid schedule is taken automatically only where it would stream at
+# most 0.6 of the cluster kernel's bytes per CTA.
 _GRID_AUTO_MAX_M = 2
-_GRID_AUTO_MAX_BYTES = 0.8
+_GRID_AUTO_MAX_BYTES = 0.6
 # (M, H, N, dtype, device) -> whether the automatic choice is the grid schedule.
 _grid_choice: dict[tuple, bool] = {}
 # Workspaces kept between calls.  Launches on one stream run in order, so calls on a

@@ -1,7 +1,7 @@
 """The Python layer's automatic choice of the grid schedule, on the CPU.
 
 ``kernel._grid_preferred`` takes ``grid`` when the rows are few (M <= 2), the library's own
-choice is the cluster decode kernel, and the grid configuration streams at most 0.8x the
+choice is the cluster decode kernel, and the grid configuration streams at most 0.6x the
 cluster configuration's weight k-blocks per CTA.  The library's schedule records are faked
 here with the configurations it reports on a 148-SM B200, so only the rule is under test.
 """
@@ -25,6 +25,7 @@ RECORDS = {
     (8192, 10240): (info(_lib.SCHED_DECODE, 2, 3, 120), info(_lib.SCHED_GRID, 4, 7, 140)),   # 86 vs 76
     (4096, 28672): (info(_lib.SCHED_DECODE, 5, 3, 135), info(_lib.SCHED_GRID, 5, 3, 135)),   # equal
     (4096, 512): (info(_lib.SCHED_SPLIT, 1, 0, 148), info(_lib.SCHED_GRID, 1, 8, 32)),       # C picks split
+    (2048, 8192): (info(_lib.SCHED_DECODE, 2, 2, 128), info(_lib.SCHED_GRID, 1, 4, 256)),   # 32 vs 8 (made up)
 }
 
 
@@ -39,11 +40,12 @@ def fake_library(monkeypatch):
 
 
 @pytest.mark.parametrize("M,H,N,expect", [
-    (1, 3584, 4608, True),     # Qwen2-7B: 14 <= 0.8 x 19 k-blocks per CTA
-    (2, 3584, 4608, True),
-    (3, 3584, 4608, False),    # above two rows
-    (1, 4096, 6144, False),    # Llama-3-8B: 22 > 0.8 x 26
-    (1, 8192, 10240, False),   # Llama-3-70B: 76 > 0.8 x 86
+    (1, 2048, 8192, True),     # a quarter of the bytes per CTA: 8 <= 0.6 x 32 k-blocks
+    (2, 2048, 8192, True),
+    (3, 2048, 8192, False),    # above two rows
+    (1, 3584, 4608, False),    # Qwen2-7B: 14 > 0.6 x 19 k-blocks per CTA
+    (1, 4096, 6144, False),    # Llama-3-8B: 22 > 0.6 x 26
+    (1, 8192, 10240, False),   # Llama-3-70B: 76 > 0.6 x 86
     (1, 4096, 28672, False),   # gate/up: the same configuration
     (1, 4096, 512, False),     # the library would not run the cluster kernel
 ])
