@@ -61,7 +61,8 @@ _ws_bytes: dict[tuple, int] = {}
 # weight bytes per CTA.  Since the cluster kernel spreads the norm phase of one to four rows
 # over all its norm warps, it beats the grid variant on every measured shape (B200,
 # graph-timed, M = 1 / 2, cluster against grid, us): Qwen2-7B 10.50 / 10.91 against 11.60 /
-# 12.23 (bytes fraction 0.74), Llama-3-8B 11.69 / 11.63 against 14.32 / 14.94 (0.85),
+# 12.23 (bytes fraction 0.74; since then the cluster kernel's two-tile stages take it to
+# 9.41 / 10.52 at M = 1 / 16), Llama-3-8B 11.69 / 11.63 against 14.32 / 14.94 (0.85),
 # Llama-3-70B 30.64 / 31.16 against 33.18 / 35.77 (0.88).  The fraction is therefore set
 # below all of them: the grid schedule is taken automatically only where it would stream at
 # most 0.6 of the cluster kernel's bytes per CTA.

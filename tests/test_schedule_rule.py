@@ -20,7 +20,7 @@ def info(schedule, nt, split, grid):
 
 # (H, N) -> (cluster record, grid record) as reported on a 148-SM B200.
 RECORDS = {
-    (3584, 4608): (info(_lib.SCHED_DECODE, 1, 3, 108), info(_lib.SCHED_GRID, 1, 4, 144)),    # 19 vs 14 k-blocks
+    (3584, 4608): (info(_lib.SCHED_DECODE, 2, 6, 108), info(_lib.SCHED_GRID, 1, 4, 144)),    # 20 vs 14 k-blocks
     (4096, 6144): (info(_lib.SCHED_DECODE, 2, 5, 120), info(_lib.SCHED_GRID, 1, 3, 144)),    # 26 vs 22
     (8192, 10240): (info(_lib.SCHED_DECODE, 2, 3, 120), info(_lib.SCHED_GRID, 4, 7, 140)),   # 86 vs 76
     (4096, 28672): (info(_lib.SCHED_DECODE, 5, 3, 135), info(_lib.SCHED_GRID, 5, 3, 135)),   # equal
@@ -43,7 +43,7 @@ def fake_library(monkeypatch):
     (1, 2048, 8192, True),     # a quarter of the bytes per CTA: 8 <= 0.6 x 32 k-blocks
     (2, 2048, 8192, True),
     (3, 2048, 8192, False),    # above two rows
-    (1, 3584, 4608, False),    # Qwen2-7B: 14 > 0.6 x 19 k-blocks per CTA
+    (1, 3584, 4608, False),    # Qwen2-7B: 14 > 0.6 x 20 k-blocks per CTA
     (1, 4096, 6144, False),    # Llama-3-8B: 22 > 0.6 x 26
     (1, 8192, 10240, False),   # Llama-3-70B: 76 > 0.6 x 86
     (1, 4096, 28672, False),   # gate/up: the same configuration
